@@ -1,0 +1,180 @@
+// Device-side building blocks of the selective-scan kernels (sm_100a).
+//
+// PTX wrappers for mbarriers, TMA tensor copies and bulk-group waits, the
+// per-element math of the four reference variants, and the shared-memory tile
+// layout. The kernels themselves are in scan_kernels.cu.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace mamba_scan {
+
+constexpr int kN = 16;     // d_state; the reference kernels support only 16 (cc:228-230)
+constexpr int kRows = 32;  // (b, d) rows per CTA: one warp, one row per lane
+constexpr int kT = 16;     // time steps per tile: 64-byte rows in shared memory
+constexpr int kStages = 2; // TMA pipeline depth
+
+enum Variant { kLinear = 0, kExact = 1, kFused = 2, kFusedExact = 3 };
+enum Mode { kEmit = 0, kAggregate = 1 };
+
+template <int V> struct VariantTraits {
+  static constexpr bool fused = (V == kFused || V == kFusedExact);
+  static constexpr bool exact = (V == kExact || V == kFusedExact);
+};
+
+// ---------------------------------------------------------------- PTX wrappers
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_mbarrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// Orders this thread's generic-proxy shared-memory accesses against later
+// async-proxy (TMA) accesses.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n"
+      "  .reg .pred p;\n"
+      "  mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      "  selp.u32 %0, 1, 0, p;\n"
+      "}\n"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait on an mbarrier phase. Gives up after ~2 s of wall time, records
+// MAMBA_SCAN_ERR_DEVICE_TIMEOUT (6) in *err and returns false, so a lost
+// transaction can never hang the GPU.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t start = globaltimer_ns();
+  for (uint32_t spins = 0;; ++spins) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((spins & 255u) == 255u && globaltimer_ns() - start > 2000000000ull) {
+      atomicExch(err, 6);
+      return false;
+    }
+  }
+}
+
+// 3-D tiled TMA load into shared memory, completing on `bar`.
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+// 3-D tiled TMA store from shared memory (out-of-range elements are clipped).
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int c0,
+                                             int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// Wait until at most N committed bulk groups still read shared memory.
+template <int N> __device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+// Wait until at most N committed bulk groups are still in flight.
+template <int N> __device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// ------------------------------------------------------------------ the math
+
+// 2^x on the SFU (PTX ex2.approx.ftz.f32).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Packed fp32x2 arithmetic (sm_100 FFMA2/FMUL2).
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+
+// softplus(x) = log(1 + e^x), with the reference's branches (cc:137-143):
+// x > 20 -> x, x < -20 -> e^x. Exact variants use IEEE expf/log1pf; the
+// approximate ones the SFU exponential and logarithm.
+template <bool kExactMath> __device__ __forceinline__ float softplus(float x) {
+  if (kExactMath) {
+    if (x > 20.f) return x;
+    if (x < -20.f) return expf(x);
+    return log1pf(expf(x));
+  } else {
+    if (x > 20.f) return x;
+    const float e = __expf(x);
+    return x < -20.f ? e : __logf(1.f + e);
+  }
+}
+
+// silu(x) = x / (1 + e^-x) (cc:145-148).
+template <bool kExactMath> __device__ __forceinline__ float silu(float x) {
+  if (kExactMath) return x / (1.f + expf(-x));
+  return __fdividef(x, 1.f + __expf(-x));
+}
+
+// Offset (in floats) of element (row, t) of a [kRows][kT] tile stored with the
+// TMA 64-byte swizzle: 16-byte chunk index t/4 XOR bits 7..8 of the row's byte
+// offset (64*row), i.e. (row >> 1) & 3.
+__device__ __forceinline__ int swz(int row, int t) {
+  return row * kT + ((((t >> 2) ^ (row >> 1)) & 3) << 2) + (t & 3);
+}
+
+// Shared memory of one CTA. Every array starts on a 1 KiB boundary so the
+// swizzle pattern is anchored at the array start.
+struct __align__(1024) TileSmem {
+  float u[kStages][kRows * kT];
+  float dl[kStages][kRows * kT];
+  float z[kStages][kRows * kT];
+  float B[kStages][kT * kN];
+  float C[kStages][kT * kN];
+  float out[2][kRows * kT];
+  uint64_t full[kStages];
+};
+
+}  // namespace mamba_scan

@@ -1,0 +1,161 @@
+"""Direct access to the CUDA selective-scan kernels through their C ABI.
+
+A thin ctypes binding of include/mamba_scan.h. Tensors are torch CUDA
+tensors (torch provides device memory and the current stream); the work runs
+in libmamba_ops_cuda.so. Importing this module on a machine without the
+library raises: there is no CPU implementation behind it.
+"""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+from . import get_library_path
+
+OPS = {
+    "SelectiveScan": 0,
+    "SelectiveScanExact": 1,
+    "SelectiveScanFused": 2,
+    "SelectiveScanFusedExact": 3,
+}
+FUSED = {"SelectiveScanFused", "SelectiveScanFusedExact"}
+
+STATUS_OK = 0
+
+
+class ScanArgs(ctypes.Structure):
+    """struct mamba_scan_args (include/mamba_scan.h)."""
+
+    _fields_ = [
+        ("u", ctypes.c_void_p),
+        ("delta", ctypes.c_void_p),
+        ("A", ctypes.c_void_p),
+        ("B", ctypes.c_void_p),
+        ("C", ctypes.c_void_p),
+        ("D", ctypes.c_void_p),
+        ("z", ctypes.c_void_p),
+        ("delta_bias", ctypes.c_void_p),
+        ("h0", ctypes.c_void_p),
+        ("out", ctypes.c_void_p),
+        ("h_last", ctypes.c_void_p),
+        ("batch", ctypes.c_int64),
+        ("dim", ctypes.c_int64),
+        ("seqlen", ctypes.c_int64),
+        ("dstate", ctypes.c_int64),
+    ]
+
+
+class ScanError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(message)
+        self.status = status
+
+
+_lib = None
+
+
+def library() -> ctypes.CDLL:
+    """Load libmamba_ops_cuda.so (once) and declare the C ABI."""
+    global _lib
+    if _lib is None:
+        lib = ctypes.CDLL(get_library_path("cuda"))
+        lib.mamba_scan_launch.restype = ctypes.c_int
+        lib.mamba_scan_launch.argtypes = [ctypes.c_int, ctypes.POINTER(ScanArgs), ctypes.c_void_p,
+                                          ctypes.c_size_t, ctypes.c_void_p]
+        lib.mamba_scan_workspace_size.restype = ctypes.c_size_t
+        lib.mamba_scan_workspace_size.argtypes = [ctypes.c_int] + [ctypes.c_int64] * 4
+        lib.mamba_scan_last_error.restype = ctypes.c_char_p
+        lib.mamba_scan_status_string.restype = ctypes.c_char_p
+        lib.mamba_scan_status_string.argtypes = [ctypes.c_int]
+        lib.mamba_scan_check_device_error.restype = ctypes.c_int
+        lib.mamba_scan_abi_version.restype = ctypes.c_int
+        _lib = lib
+    return _lib
+
+
+def library_path() -> Path:
+    return Path(get_library_path("cuda"))
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _check(name, t, shape):
+    import torch
+
+    if t is None:
+        return
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise TypeError(f"{name} must be a CUDA tensor")
+    if t.dtype != torch.float32:
+        raise TypeError(f"{name} must be float32, got {t.dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    if tuple(t.shape) != tuple(shape):
+        raise ValueError(f"{name} must have shape {tuple(shape)}, got {tuple(t.shape)}")
+
+
+def workspace_size(op: str, batch: int, dim: int, seqlen: int, dstate: int = 16) -> int:
+    return int(library().mamba_scan_workspace_size(OPS[op], batch, dim, seqlen, dstate))
+
+
+def selective_scan(op: str, u, delta, A, B, C, D, z=None, *, delta_bias=None, h0=None,
+                   out=None, h_last=None, workspace=None, chunked=True, stream=None):
+    """Run one selective-scan op on CUDA tensors; returns ``out`` ([batch, dim, seqlen]).
+
+    op: one of the four reference op names. Layouts: u/delta/z [B,D,L], A [D,N],
+    B/C [B,L,N], D [D]; optional delta_bias [D] (fused ops), h0 / h_last [B,D,N].
+    workspace: optional uint8 CUDA tensor; by default one of
+    workspace_size(...) bytes is taken from torch's allocator.
+    chunked: False passes no workspace, so the sequence runs as one pass.
+    stream: a torch.cuda.Stream (default: the current stream).
+    """
+    import torch
+
+    if op not in OPS:
+        raise ValueError(f"unknown op {op!r}")
+    if u.dim() != 3 or A.dim() != 2:
+        raise ValueError("u must be [batch, dim, seqlen] and A [dim, dstate]")
+    batch, dim, seqlen = u.shape
+    dstate = A.shape[1]
+    for name, t, shape in [("u", u, (batch, dim, seqlen)), ("delta", delta, (batch, dim, seqlen)),
+                           ("A", A, (dim, dstate)), ("B", B, (batch, seqlen, dstate)),
+                           ("C", C, (batch, seqlen, dstate)), ("D", D, (dim,)),
+                           ("z", z, (batch, dim, seqlen)), ("delta_bias", delta_bias, (dim,)),
+                           ("h0", h0, (batch, dim, dstate)), ("h_last", h_last, (batch, dim, dstate))]:
+        _check(name, t, shape)
+    if op in FUSED and z is None:
+        raise ValueError(f"{op} needs z")
+    if out is None:
+        out = torch.empty((batch, dim, seqlen), dtype=torch.float32, device=u.device)
+    else:
+        _check("out", out, (batch, dim, seqlen))
+    lib = library()
+    ws_bytes = int(lib.mamba_scan_workspace_size(OPS[op], batch, dim, seqlen, dstate))
+    if not chunked:
+        workspace = None
+    elif workspace is None and ws_bytes > 0:
+        workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=u.device)
+    args = ScanArgs(_ptr(u), _ptr(delta), _ptr(A), _ptr(B), _ptr(C), _ptr(D),
+                    _ptr(z) if op in FUSED else None, _ptr(delta_bias), _ptr(h0), _ptr(out),
+                    _ptr(h_last), batch, dim, seqlen, dstate)
+    st = stream if stream is not None else torch.cuda.current_stream(u.device)
+    rc = lib.mamba_scan_launch(OPS[op], ctypes.byref(args), _ptr(workspace),
+                               0 if workspace is None else workspace.numel(), st.cuda_stream)
+    if rc != STATUS_OK:
+        raise ScanError(rc, f"{op}: {lib.mamba_scan_status_string(rc).decode()}: "
+                            f"{lib.mamba_scan_last_error().decode()}")
+    return out
+
+
+def launch_raw(op_id: int, args: ScanArgs, workspace_ptr, workspace_bytes: int,
+               stream_handle) -> int:
+    """Call mamba_scan_launch with a prepared argument struct; returns the status."""
+    return int(library().mamba_scan_launch(op_id, ctypes.byref(args), workspace_ptr,
+                                           workspace_bytes, stream_handle))
+
+
+def check_device_error() -> int:
+    """Synchronise and return/clear the kernels' device error word (0 = none)."""
+    return int(library().mamba_scan_check_device_error())

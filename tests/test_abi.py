@@ -1,0 +1,204 @@
+"""CPU: the built library, its C ABI, the ORT op table and the Python loader.
+
+No kernel is launched here (there is no GPU in the build container); every
+call below returns before the library touches CUDA.
+"""
+import ctypes
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import mamba_onnx
+from fake_ort import ort_shim
+from mamba_onnx import cuda
+
+ROOT = Path(__file__).resolve().parent.parent
+HEADERS = sorted((ROOT / "include").glob("*.h"))
+
+
+def declared_functions():
+    names = set()
+    for h in HEADERS:
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        text = re.sub(r"^\s*#.*$", "", text, flags=re.M)
+        text = re.sub(r"__attribute__\s*\(\(.*?\)\)", "", text)
+        for m in re.finditer(r"\b([A-Za-z_][A-Za-z0-9_]*)\s*\(([^;{}]*)\)\s*;", text):
+            name = m.group(1)
+            if name not in {"defined", "__attribute__", "visibility"}:
+                names.add(name)
+    return names
+
+
+def test_headers_declare_the_boundary():
+    names = declared_functions()
+    assert {"RegisterCustomOps", "mamba_scan_launch", "mamba_scan_workspace_size",
+            "mamba_scan_last_error", "mamba_scan_status_string",
+            "mamba_scan_check_device_error", "mamba_scan_abi_version"} <= names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(str(cuda.library_path()))
+    for name in declared_functions():
+        assert hasattr(lib, name), f"{name} declared in include/ but not exported"
+
+
+def test_abi_version_and_status_strings():
+    lib = cuda.library()
+    assert lib.mamba_scan_abi_version() == 1
+    assert lib.mamba_scan_status_string(2) == b"unsupported dstate"
+    assert lib.mamba_scan_status_string(99) == b"unknown status"
+
+
+def _args(**kw):
+    a = cuda.ScanArgs()
+    fake = 0x10000  # never dereferenced: these calls fail validation first
+    for f in ("u", "delta", "A", "B", "C", "D", "z", "out"):
+        setattr(a, f, fake * (1 + len(f)))
+    a.batch, a.dim, a.seqlen, a.dstate = 1, 64, 32, 16
+    for k, v in kw.items():
+        setattr(a, k, v)
+    return a
+
+
+@pytest.mark.parametrize("kw,variant,status,msg", [
+    (dict(dstate=8), 0, 2, "dstate=16"),
+    (dict(), 7, 1, "variant"),
+    (dict(seqlen=-1), 0, 1, "negative"),
+    (dict(u=None), 1, 1, "non-NULL"),
+    (dict(z=None), 2, 1, "need z"),
+])
+def test_launch_rejects_bad_arguments_before_any_cuda_call(kw, variant, status, msg):
+    lib = cuda.library()
+    rc = lib.mamba_scan_launch(variant, ctypes.byref(_args(**kw)), None, 0, None)
+    assert rc == status
+    assert msg in lib.mamba_scan_last_error().decode()
+
+
+def test_launch_rejects_aliasing_output():
+    lib = cuda.library()
+    a = _args()
+    a.out = a.u
+    assert lib.mamba_scan_launch(0, ctypes.byref(a), None, 0, None) == 4
+
+
+def test_empty_batch_is_a_no_op():
+    lib = cuda.library()
+    assert lib.mamba_scan_launch(0, ctypes.byref(_args(batch=0)), None, 0, None) == 0
+
+
+# ---- Python loader (mirror of the reference's src/mamba_onnx/__init__.py) ----
+
+def test_loader_lists_cuda_backend():
+    assert "cuda" in mamba_onnx.available_backends()
+    assert mamba_onnx.get_library_path("cuda").endswith("libmamba_ops_cuda.so")
+    assert mamba_onnx.get_library_path("auto") == mamba_onnx.get_library_path("cuda")
+
+
+def test_loader_has_no_cpu_fallback():
+    with pytest.raises(FileNotFoundError):
+        mamba_onnx.get_library_path("cpp")
+    with pytest.raises(ValueError):
+        mamba_onnx.get_library_path("metal")
+
+
+def test_register_custom_ops_passes_the_library_to_the_session_options():
+    class Opts:
+        def __init__(self):
+            self.paths = []
+
+        def register_custom_ops_library(self, path):
+            self.paths.append(path)
+
+    opts = Opts()
+    path = mamba_onnx.register_custom_ops(opts, backend="cuda")
+    assert opts.paths == [path] and path.endswith("libmamba_ops_cuda.so")
+
+
+# ---- ORT op table through the fake CUDA-EP host ----
+
+def test_op_table_matches_reference_ops():
+    opts = ort_shim.SessionOptions()
+    mamba_onnx.register_custom_ops(opts, backend="cuda")
+    infos = {i.name: i for i in ort_shim.op_infos(opts.libraries[0])}
+    # selective_scan.cc:332-371: names, input counts, one float output, opset 1..INT_MAX
+    assert list(infos) == ["SelectiveScan", "SelectiveScanExact", "SelectiveScanFused",
+                           "SelectiveScanFusedExact"]
+    for name, info in infos.items():
+        assert info.ep == "CUDAExecutionProvider"
+        assert info.n_outputs == 1 and info.version_range == (1, 2147483647)
+        assert info.has_v2
+    assert infos["SelectiveScan"].input_characteristics == "R" * 6
+    assert infos["SelectiveScanExact"].input_characteristics == "R" * 6
+    assert infos["SelectiveScanFused"].input_characteristics == "R" * 7 + "O"
+    assert infos["SelectiveScanFusedExact"].input_characteristics == "R" * 7 + "O"
+
+
+def test_register_failure_is_reported_not_swallowed():
+    ort_shim.fail_next("CustomOpDomain_Add")
+    with pytest.raises(ort_shim.OrtError, match="injected failure in CustomOpDomain_Add"):
+        ort_shim.load_library(mamba_onnx.get_library_path("cuda"))
+
+
+def _session(op):
+    opts = ort_shim.SessionOptions()
+    mamba_onnx.register_custom_ops(opts, backend="cuda")
+    fused = "Fused" in op
+    return ort_shim.InferenceSession(ort_shim.make_model(op, fused), opts,
+                                     providers=["CUDAExecutionProvider"])
+
+
+def _fake_run(sess, shapes, types=None, out_shape=(1, 64, 32)):
+    """Drive the op with fake device pointers; validation must fail first."""
+    h = ort_shim.host()
+    n = len(shapes)
+    ptrs = (ctypes.c_void_p * n)(*[0x100000 * (i + 1) for i in range(n)])
+    dims = [d for s in shapes for d in s]
+    ranks = (ctypes.c_int * n)(*[len(s) for s in shapes])
+    tys = (ctypes.c_int * n)(*(types or [1] * n))
+    err = ctypes.create_string_buffer(1024)
+    rc = h.fake_ort_run(sess.lib, sess.model.op_type.encode(), n, ptrs,
+                        (ctypes.c_int64 * len(dims))(*dims), ranks, tys, 0x900000,
+                        (ctypes.c_int64 * 3)(*out_shape), 3, None, 1, err, len(err))
+    return rc, err.value.decode()
+
+
+GOOD = [(1, 64, 32), (1, 64, 32), (64, 16), (1, 32, 16), (1, 32, 16), (64,)]
+
+
+@pytest.mark.parametrize("shapes,types,msg", [
+    ([(64, 32)] + GOOD[1:], None, "u must be"),
+    (GOOD[:2] + [(64, 8)] + [(1, 32, 8), (1, 32, 8), (64,)], None, "Only dstate=16"),
+    (GOOD[:3] + [(1, 31, 16)] + GOOD[4:], None, "B and C"),
+    (GOOD[:5] + [(63,)], None, "D must be"),
+    (GOOD, [1, 11, 1, 1, 1, 1], "float32"),
+    (GOOD[:5], None, "expected 6 inputs"),
+])
+def test_ort_layer_validates_before_launch(shapes, types, msg):
+    rc, err = _fake_run(_session("SelectiveScan"), shapes, types)
+    assert rc == 2, err  # ORT_INVALID_ARGUMENT
+    assert msg in err
+
+
+def test_ort_layer_propagates_host_failures():
+    sess = _session("SelectiveScan")
+    for api in ["KernelContext_GetInput", "KernelContext_GetOutput", "GetTensorTypeAndShape",
+                "KernelContext_GetGPUComputeStream"]:
+        ort_shim.fail_next(api)
+        rc, err = _fake_run(sess, GOOD)
+        assert rc == 1 and f"injected failure in {api}" in err
+
+
+def test_ort_layer_fused_delta_bias_shape_checked():
+    sess = _session("SelectiveScanFused")
+    sess.model.inputs.append("delta_bias")
+    rc, err = _fake_run(sess, GOOD + [(1, 64, 32), (63,)])
+    assert rc == 2 and "delta_bias" in err
+
+
+def test_workspace_size_is_zero_without_chunking():
+    # Large row counts run as one pass; tiny sequences never split.
+    assert cuda.workspace_size("SelectiveScanFused", 8, 5120, 2048) == 0
+    assert cuda.workspace_size("SelectiveScan", 1, 64, 32) == 0
+    assert np.int64(cuda.workspace_size("SelectiveScanExact", 1, 2048, 16384)) > 0
