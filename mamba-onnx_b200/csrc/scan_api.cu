@@ -45,32 +45,76 @@ int sm_count(int device) {
 }
 
 struct Plan {
+  int64_t n_full = 0;  // row tiles scanned in one pass
+  int64_t n_tail = 0;  // row tiles split into chunks
   int n_chunks = 1;
   int64_t chunk_len = 0;
 };
 
-// Single pass while there are at least 4 row tiles (warps) per SM; otherwise
-// split the sequence so that row tiles x chunks reaches ~8 warps per SM.
-// Chunks are multiples of 32 steps (two tiles), so every chunk but the last
-// starts and ends on a tile boundary.
-Plan make_plan(int64_t batch, int64_t dim, int64_t seqlen, int sms) {
+int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
+
+// Plan for a kernel that fits `slots` one-warp CTAs per SM.
+//
+// A row tile runs fastest with at most two warps on each of the SM's four
+// sub-partitions (it is then latency-bound; more warps only share the
+// sub-partition's issue slots), and a CTA that ends frees its slot for the
+// next one. So the plan thinks in waves of slots x SMs CTAs:
+// * fewer row tiles than sub-partitions: every row tile is split into
+//   sequence chunks so that row tiles x chunks gives about two warps per
+//   sub-partition, within one wave;
+// * otherwise full waves of row tiles run in one pass, and a last, partial
+//   wave of R row tiles (if small enough) is split into c chunks, about one
+//   per sub-partition: the tail then costs an aggregate pass and a chunk
+//   pass of ~1/c of a row tile each instead of a whole row tile.
+// Chunks are multiples of 32 steps, so every chunk but the last starts and
+// ends on a tile boundary.
+Plan make_plan(int64_t batch, int64_t dim, int64_t seqlen, int sms, int slots) {
   Plan pl;
+  const int64_t N = batch * ((dim + kRows - 1) / kRows);
+  const int64_t subparts = 4LL * sms;
+  const int64_t wave = std::max<int64_t>(1, (int64_t)slots * sms);
+  pl.n_full = N;
   pl.chunk_len = seqlen;
-  const int64_t tiles = batch * ((dim + kRows - 1) / kRows);
-  if (tiles <= 0 || seqlen <= 2 * kMinChunk || tiles >= 4LL * sms) return pl;
-  const int64_t want = (8LL * sms + tiles - 1) / tiles;
-  int64_t len = (seqlen + want - 1) / want;
-  len = std::max<int64_t>(kMinChunk, (len + kMinChunk - 1) / kMinChunk * kMinChunk);
+  if (N <= 0 || seqlen <= 2 * kMinChunk) return pl;
+  int64_t tail = 0, want = 0;
+  if (N < subparts) {
+    tail = N;
+    want = std::min((2 * subparts + N - 1) / N, std::max<int64_t>(1, wave / N));
+  } else {
+    tail = N % wave;
+    if (N < wave || tail == 0) return pl;
+    // about one chunk per sub-partition; below 3 chunks the aggregate pass
+    // and the per-chunk start-up cost more than they save
+    want = subparts / tail;
+    if (want < 3) return pl;
+  }
+  int64_t len = round_up((seqlen + want - 1) / want, kMinChunk);
+  len = std::max<int64_t>(len, 2 * kMinChunk);
   const int64_t n = (seqlen + len - 1) / len;
-  if (n <= 1 || n > 65535) return pl;
+  if (n < 2 || n > 4096) return pl;
+  pl.n_full = N - tail;
+  pl.n_tail = tail;
   pl.n_chunks = (int)n;
   pl.chunk_len = len;
   return pl;
 }
 
-size_t workspace_bytes_for(const Plan& pl, int64_t batch, int64_t dim) {
-  if (pl.n_chunks <= 1) return 0;
-  return (size_t)batch * (size_t)dim * (size_t)(pl.n_chunks - 1) * 32 * sizeof(float);
+// Resident emit CTAs per SM for a variant (cached per device).
+int emit_slots(int device, int variant, bool tma) {
+  static std::atomic<int> cache[64][4][2];
+  if (device < 0 || device >= 64 || variant < 0 || variant > 3) return 8;
+  int v = cache[device][variant][tma ? 1 : 0].load(std::memory_order_relaxed);
+  if (v > 0) return v;
+  if (mamba_scan::max_blocks_per_sm(variant, mamba_scan::kLaunchEmit, tma, &v) != cudaSuccess ||
+      v <= 0)
+    v = 8;
+  cache[device][variant][tma ? 1 : 0].store(v, std::memory_order_relaxed);
+  return v;
+}
+
+size_t workspace_bytes_for(const Plan& pl) {
+  if (pl.n_tail == 0 || pl.n_chunks <= 1) return 0;
+  return (size_t)pl.n_tail * kRows * (size_t)(pl.n_chunks - 1) * 32 * sizeof(float);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -133,7 +177,8 @@ size_t mamba_scan_workspace_size(int variant, int64_t batch, int64_t dim, int64_
     return 0;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
-  return workspace_bytes_for(make_plan(batch, dim, seqlen, sm_count(dev)), batch, dim);
+  return workspace_bytes_for(
+      make_plan(batch, dim, seqlen, sm_count(dev), emit_slots(dev, variant, true)));
 }
 
 int mamba_scan_launch(int variant, const mamba_scan_args* a, void* workspace,
@@ -149,8 +194,9 @@ int mamba_scan_launch(int variant, const mamba_scan_args* a, void* workspace,
     return fail(MAMBA_SCAN_ERR_UNSUPPORTED_DSTATE,
                 "Only dstate=16 is supported in this kernel (got " + std::to_string(a->dstate) +
                     ")");
-  if (a->dim > (int64_t)1 << 31 || a->batch > (int64_t)1 << 31 || a->seqlen > (int64_t)1 << 31)
-    return fail(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "dimension exceeds 2^31");
+  if (a->dim > (int64_t)1 << 31 || a->batch > (int64_t)1 << 31 || a->seqlen > (int64_t)1 << 31 ||
+      a->batch * ((a->dim + kRows - 1) / kRows) * 64 > (int64_t)1 << 31)
+    return fail(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "dimension exceeds 2^31 (or batch x dim too large)");
   const int64_t B = a->batch, D = a->dim, L = a->seqlen;
   if (B == 0 || D == 0) return MAMBA_SCAN_OK;  // empty output
   if (!a->A || !a->D) return fail(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "A and D must be non-NULL");
@@ -187,25 +233,6 @@ int mamba_scan_launch(int variant, const mamba_scan_args* a, void* workspace,
   if (overlaps(a->out, big, a->h_last, state_bytes))
     return fail(MAMBA_SCAN_ERR_ALIASING, "h_last overlaps out");
 
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return fail(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
-  Plan pl = make_plan(B, D, L, sm_count(dev));
-  const size_t need = workspace_bytes_for(pl, B, D);
-  if (need > 0) {
-    if (workspace == nullptr) {
-      pl = Plan{1, L};  // no workspace: run the sequence as one pass
-    } else if (workspace_bytes < need) {
-      return fail(MAMBA_SCAN_ERR_WORKSPACE, "workspace holds " + std::to_string(workspace_bytes) +
-                                                " bytes; this shape needs " +
-                                                std::to_string(need));
-    } else if (!aligned16(workspace)) {
-      return fail(MAMBA_SCAN_ERR_WORKSPACE, "workspace must be 16-byte aligned");
-    } else if (overlaps(workspace, need, a->out, big)) {
-      return fail(MAMBA_SCAN_ERR_ALIASING, "workspace overlaps out");
-    }
-  }
-
   ScanParams p{};
   p.u = a->u;
   p.delta = a->delta;
@@ -218,13 +245,14 @@ int mamba_scan_launch(int variant, const mamba_scan_args* a, void* workspace,
   p.h0 = a->h0;
   p.out = a->out;
   p.h_last = a->h_last;
-  p.ws = static_cast<float*>(workspace);
   p.batch = B;
   p.dim = D;
   p.seqlen = L;
-  p.chunk_len = pl.chunk_len;
   p.tiles_per_batch = (int)((D + kRows - 1) / kRows);
-  p.n_chunks = pl.n_chunks;
+
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
 
   // TMA needs 16-byte aligned bases and 16-byte multiple strides (L % 4 == 0).
   TmaMaps maps;
@@ -240,14 +268,37 @@ int mamba_scan_launch(int variant, const mamba_scan_args* a, void* workspace,
           encode_bc(enc, &maps.C, a->C, B, L);
   }
 
-  const unsigned row_tiles = (unsigned)(B * p.tiles_per_batch);
-  if (pl.n_chunks > 1) {
+  // (planned with the TMA kernel's occupancy, as mamba_scan_workspace_size does)
+  Plan pl = make_plan(B, D, L, sm_count(dev), emit_slots(dev, variant, true));
+  const size_t need = workspace_bytes_for(pl);
+  if (need > 0) {
+    if (workspace == nullptr) {
+      pl = Plan{};  // no workspace: every row tile runs as one pass
+      pl.n_full = B * ((D + kRows - 1) / kRows);
+      pl.chunk_len = L;
+    } else if (workspace_bytes < need) {
+      return fail(MAMBA_SCAN_ERR_WORKSPACE, "workspace holds " + std::to_string(workspace_bytes) +
+                                                " bytes; this shape needs " +
+                                                std::to_string(need));
+    } else if (!aligned16(workspace)) {
+      return fail(MAMBA_SCAN_ERR_WORKSPACE, "workspace must be 16-byte aligned");
+    } else if (overlaps(workspace, need, a->out, big)) {
+      return fail(MAMBA_SCAN_ERR_ALIASING, "workspace overlaps out");
+    }
+  }
+
+  p.ws = static_cast<float*>(workspace);
+  p.chunk_len = pl.chunk_len;
+  p.n_full = (int)pl.n_full;
+  p.n_tail = (int)pl.n_tail;
+  p.n_chunks = pl.n_chunks;
+  if (pl.n_tail > 0 && pl.n_chunks > 1) {
     e = mamba_scan::launch_scan_kernel(variant, mamba_scan::kLaunchAggregate, tma, p, maps,
-                                       dim3(row_tiles, (unsigned)(pl.n_chunks - 1)), st);
+                                       (unsigned)(pl.n_tail * (pl.n_chunks - 1)), st);
     if (e != cudaSuccess) return fail(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
   }
   e = mamba_scan::launch_scan_kernel(variant, mamba_scan::kLaunchEmit, tma, p, maps,
-                                     dim3(row_tiles, (unsigned)pl.n_chunks), st);
+                                     (unsigned)(pl.n_full + pl.n_tail * pl.n_chunks), st);
   if (e != cudaSuccess) return fail(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
   return MAMBA_SCAN_OK;
 }

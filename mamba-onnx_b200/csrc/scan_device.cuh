@@ -14,7 +14,7 @@ namespace mamba_scan {
 constexpr int kN = 16;     // d_state; the reference kernels support only 16 (cc:228-230)
 constexpr int kRows = 32;  // (b, d) rows per CTA: one warp, one row per lane
 constexpr int kT = 16;     // time steps per tile: 64-byte rows in shared memory
-constexpr int kStages = 2; // TMA pipeline depth
+constexpr int kStages = 3;  // tiles in the shared-memory ring
 
 enum Variant { kLinear = 0, kExact = 1, kFused = 2, kFusedExact = 3 };
 enum Mode { kEmit = 0, kAggregate = 1 };
@@ -136,26 +136,46 @@ __device__ __forceinline__ float ex2_approx(float x) {
 // Packed fp32x2 arithmetic (sm_100 FFMA2/FMUL2).
 __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
 __device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
 
-// softplus(x) = log(1 + e^x), with the reference's branches (cc:137-143):
-// x > 20 -> x, x < -20 -> e^x. Exact variants use IEEE expf/log1pf; the
-// approximate ones the SFU exponential and logarithm.
-template <bool kExactMath> __device__ __forceinline__ float softplus(float x) {
+__device__ __forceinline__ float lg2_approx(float x) {
+  float y;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// softplus(x + bias) = log(1 + e^(x+bias)).
+// Exact variants: IEEE expf/log1pf with the reference's branches
+// (cc:137-143: x > 20 -> x, x < -20 -> e^x).
+// Approximate variants: SFU 2^x and log2 on s = (x + bias) * log2(e), formed
+// by one FMA with bias_l2e = bias * log2(e); s > 20*log2(e) returns x + bias.
+// Below x = -20 this gives log(1 + e^x) rounded in fp32 (0 once e^x < 2^-24)
+// instead of e^x: an absolute difference under 2.1e-9.
+template <bool kExactMath>
+__device__ __forceinline__ float softplus(float x, float bias, float bias_l2e) {
   if (kExactMath) {
+    x += bias;
     if (x > 20.f) return x;
     if (x < -20.f) return expf(x);
     return log1pf(expf(x));
   } else {
-    if (x > 20.f) return x;
-    const float e = __expf(x);
-    return x < -20.f ? e : __logf(1.f + e);
+    const float s = fmaf(x, 1.4426950408889634f, bias_l2e);
+    const float l = lg2_approx(1.f + ex2_approx(s));
+    return (s > 28.853900817779268f ? s : l) * 0.6931471805599453f;
   }
 }
 
-// silu(x) = x / (1 + e^-x) (cc:145-148).
+// silu(x) = x / (1 + e^-x) (cc:145-148); approximate variants use the SFU
+// 2^x and reciprocal.
 template <bool kExactMath> __device__ __forceinline__ float silu(float x) {
   if (kExactMath) return x / (1.f + expf(-x));
-  return __fdividef(x, 1.f + __expf(-x));
+  return x * rcp_approx(1.f + ex2_approx(x * -1.4426950408889634f));
 }
 
 // Offset (in floats) of element (row, t) of a [kRows][kT] tile stored with the
@@ -165,15 +185,16 @@ __device__ __forceinline__ int swz(int row, int t) {
   return row * kT + ((((t >> 2) ^ (row >> 1)) & 3) << 2) + (t & 3);
 }
 
-// Shared memory of one CTA. Every array starts on a 1 KiB boundary so the
-// swizzle pattern is anchored at the array start.
+// Shared memory of one CTA: a ring of kStages tiles. The outputs of a tile
+// are written over its u tile, which the TMA store then reads; the stage is
+// refilled one tile later, once that store has left shared memory. Every
+// array starts on a 1 KiB boundary so the swizzle is anchored at its start.
 struct __align__(1024) TileSmem {
   float u[kStages][kRows * kT];
   float dl[kStages][kRows * kT];
   float z[kStages][kRows * kT];
   float B[kStages][kT * kN];
   float C[kStages][kT * kN];
-  float out[2][kRows * kT];
   uint64_t full[kStages];
 };
 

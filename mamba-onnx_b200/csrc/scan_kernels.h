@@ -20,12 +20,19 @@ struct ScanParams {
   const float* h0;
   float* out;
   float* h_last;
-  float* ws;  // chunk aggregates: [B*D][n_chunks-1][32] (16 states, 16 decays)
+  float* ws;  // chunk aggregates: [n_tail*32 rows][n_chunks-1][32] (16 states, 16 decays)
   int64_t batch;
   int64_t dim;
   int64_t seqlen;
-  int64_t chunk_len;    // multiple of 32, or seqlen for a single pass
+  // Work plan over the B*ceil(D/32) row tiles (32 rows each): row tiles
+  // [0, n_full) are scanned in one pass over the whole sequence; row tiles
+  // [n_full, n_full + n_tail) are split into n_chunks chunks of chunk_len
+  // steps (the last chunk takes the rest) that run in parallel: an aggregate
+  // launch over chunks 0..n_chunks-2, then the emit launch.
+  int64_t chunk_len;    // multiple of 32
   int tiles_per_batch;  // ceil(dim / 32)
+  int n_full;
+  int n_tail;
   int n_chunks;
 };
 
@@ -38,9 +45,13 @@ struct TmaMaps {
 enum LaunchMode { kLaunchEmit = 0, kLaunchAggregate = 1 };
 
 // Enqueue one scan kernel (variant 0..3, mode, TMA or plain-load tile path)
-// on `stream` with grid (row_tiles, chunks).
+// on `stream` with a 1-D grid of `blocks` CTAs: n_full + n_tail * n_chunks
+// for emit, n_tail * (n_chunks - 1) for aggregate.
 cudaError_t launch_scan_kernel(int variant, int mode, bool tma, const ScanParams& p,
-                               const TmaMaps& maps, dim3 grid, cudaStream_t stream);
+                               const TmaMaps& maps, unsigned blocks, cudaStream_t stream);
+
+// Resident CTAs per SM of one kernel instantiation (occupancy calculator).
+cudaError_t max_blocks_per_sm(int variant, int mode, bool tma, int* blocks);
 
 // Device error word accessors (see mamba_scan_check_device_error).
 cudaError_t read_and_clear_device_error(int* code);

@@ -197,8 +197,18 @@ def test_ort_layer_fused_delta_bias_shape_checked():
     assert rc == 2 and "delta_bias" in err
 
 
-def test_workspace_size_is_zero_without_chunking():
-    # Large row counts run as one pass; tiny sequences never split.
-    assert cuda.workspace_size("SelectiveScanFused", 8, 5120, 2048) == 0
+def test_workspace_plan():
+    """Workspace is needed exactly when some row tiles are split into chunks.
+
+    Off the GPU the planner assumes 148 SMs and 8 resident CTAs per SM, i.e.
+    waves of 1184 row tiles.
+    """
+    # 37 x 1024 rows = 1184 row tiles = one full wave: one pass, no workspace
+    assert cuda.workspace_size("SelectiveScanFused", 37, 1024, 2048) == 0
+    # short sequences never split
     assert cuda.workspace_size("SelectiveScan", 1, 64, 32) == 0
-    assert np.int64(cuda.workspace_size("SelectiveScanExact", 1, 2048, 16384)) > 0
+    # 8 x 5120 rows = 1280 row tiles: the 96 past one wave are split into
+    # 6 chunks of 352 steps: 96 * 32 rows * 5 aggregates * 32 floats
+    assert cuda.workspace_size("SelectiveScanFused", 8, 5120, 2048) == 96 * 32 * 5 * 32 * 4
+    # few row tiles, long sequence: everything is split
+    assert cuda.workspace_size("SelectiveScanExact", 1, 2048, 16384) > 0
