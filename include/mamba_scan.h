@@ -99,6 +99,29 @@ MAMBA_SCAN_API size_t mamba_scan_workspace_size(int variant, int64_t batch, int6
 MAMBA_SCAN_API int mamba_scan_launch(int variant, const mamba_scan_args* args, void* workspace,
                       size_t workspace_bytes, void* stream);
 
+/*
+ * Same as mamba_scan_launch, for callers that cannot allocate device memory
+ * (a runtime whose memory planner owns every buffer, a launch path that must
+ * not call cudaMalloc, an FFI caller without a device allocator). It takes no
+ * workspace: the scratch that long-sequence shapes need comes from an array
+ * compiled into the library, MAMBA_SCAN_STATIC_WORKSPACE_BYTES bytes per GPU,
+ * held from the moment the library's kernels are loaded on that GPU until the
+ * process exits. It allocates nothing and calls no allocating routine.
+ *
+ * - Shapes that need more scratch than that (see mamba_scan_workspace_size)
+ *   are rejected with MAMBA_SCAN_ERR_WORKSPACE; nothing is enqueued.
+ * - The first call on a device looks up the array's address on that device
+ *   (cudaGetSymbolAddress), so make it before any stream capture.
+ * - Every call on a device uses the same array. Calls whose work can overlap
+ *   on the GPU (different streams without ordering between them, several
+ *   host threads) race on it; order them on one stream. No call depends on
+ *   what an earlier call left in the array.
+ * The reference has no counterpart: its CPU kernel needs no scratch.
+ */
+#define MAMBA_SCAN_STATIC_WORKSPACE_BYTES (8u << 20)
+MAMBA_SCAN_API int mamba_scan_launch_static_workspace(int variant, const mamba_scan_args* args,
+                                                      void* stream);
+
 /* Message for the calling thread's most recent failed call ("" if none). */
 MAMBA_SCAN_API const char* mamba_scan_last_error(void);
 

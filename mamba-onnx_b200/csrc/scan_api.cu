@@ -169,6 +169,10 @@ bool is_fused(int v) { return v == MAMBA_SCAN_FUSED || v == MAMBA_SCAN_FUSED_EXA
 
 }  // namespace
 
+namespace mamba_scan {
+int set_last_error(int status, const std::string& msg) { return fail(status, msg); }
+}  // namespace mamba_scan
+
 extern "C" {
 
 size_t mamba_scan_workspace_size(int variant, int64_t batch, int64_t dim, int64_t seqlen,

@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <string>
+
 namespace mamba_scan {
 
 // Everything a scan kernel reads, besides the TMA descriptors.
@@ -52,6 +54,9 @@ cudaError_t launch_scan_kernel(int variant, int mode, bool tma, const ScanParams
 
 // Resident CTAs per SM of one kernel instantiation (occupancy calculator).
 cudaError_t max_blocks_per_sm(int variant, int mode, bool tma, int* blocks);
+
+// Record `msg` as the calling thread's mamba_scan_last_error(); returns status.
+int set_last_error(int status, const std::string& msg);
 
 // Device error word accessors (see mamba_scan_check_device_error).
 cudaError_t read_and_clear_device_error(int* code);

@@ -69,6 +69,9 @@ def library() -> ctypes.CDLL:
         lib.mamba_scan_status_string.argtypes = [ctypes.c_int]
         lib.mamba_scan_check_device_error.restype = ctypes.c_int
         lib.mamba_scan_abi_version.restype = ctypes.c_int
+        lib.mamba_scan_launch_static_workspace.restype = ctypes.c_int
+        lib.mamba_scan_launch_static_workspace.argtypes = [ctypes.c_int, ctypes.POINTER(ScanArgs),
+                                                           ctypes.c_void_p]
         _lib = lib
     return _lib
 
@@ -154,6 +157,17 @@ def launch_raw(op_id: int, args: ScanArgs, workspace_ptr, workspace_bytes: int,
     """Call mamba_scan_launch with a prepared argument struct; returns the status."""
     return int(library().mamba_scan_launch(op_id, ctypes.byref(args), workspace_ptr,
                                            workspace_bytes, stream_handle))
+
+
+def launch_static_workspace(op_id: int, args: ScanArgs, stream_handle) -> int:
+    """Call mamba_scan_launch_static_workspace: the scan with no device allocation.
+
+    For callers that cannot allocate device memory; the scratch of long-sequence
+    shapes comes from a fixed array inside the library (include/mamba_scan.h
+    states its size and its rules). Returns the status.
+    """
+    return int(library().mamba_scan_launch_static_workspace(op_id, ctypes.byref(args),
+                                                            stream_handle))
 
 
 def check_device_error() -> int:
