@@ -224,6 +224,8 @@ def main():
     ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ncu-case", action="store_true",
+                    help="for profilers: build the inputs, run warmup+steps calls, print nothing timed")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
@@ -252,7 +254,7 @@ def main():
 
     # CPU baseline first (rank 0, one GPU only): it must not overlap the GPU timing.
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not (args.no_cpu_baseline or args.ncu_case):
         from oracle import oracle
 
         cpu = reference_sample(oracle.host_threads(), reps=5)
@@ -266,6 +268,14 @@ def main():
 
     def step():
         cuda.selective_scan(OP, u, delta, A, Bm, Cm, Dv, z, out=out, workspace=ws, stream=stream)
+
+    if args.ncu_case:
+        for _ in range(args.warmup + args.steps):
+            step()
+        torch.cuda.synchronize()
+        print(json.dumps({"ncu_case": WORKLOAD, "launches_per_call": launches_per_step,
+                          "calls": args.warmup + args.steps}))
+        return
 
     for _ in range(args.warmup):
         step()
@@ -314,6 +324,7 @@ def main():
             "gpu_launches": launches_per_step * args.steps,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                          "frac": achieved / hbm_peak, "traffic": traffic,
+                         "per": "op call (aggregate + emit launches when the plan splits)",
                          "peak_source": f"{peak_kind} hbm_gbs",
                          "algorithmic_bytes_per_launch": algo,
                          "sfu_ops_per_launch": sfu_ops(BATCH, DIM, SEQLEN)},
