@@ -296,13 +296,19 @@ int mamba_scan_launch(int variant, const mamba_scan_args* a, void* workspace,
   p.n_full = (int)pl.n_full;
   p.n_tail = (int)pl.n_tail;
   p.n_chunks = pl.n_chunks;
-  if (pl.n_tail > 0 && pl.n_chunks > 1) {
+  // Split plan: aggregate pass, carry kernel, emit pass. The last two are
+  // programmatic dependent launches, so the emit pass's whole row tiles run
+  // alongside the aggregate pass; its chunk CTAs wait for the carry kernel.
+  const bool split = pl.n_tail > 0 && pl.n_chunks > 1;
+  if (split) {
     e = mamba_scan::launch_scan_kernel(variant, mamba_scan::kLaunchAggregate, tma, p, maps,
-                                       (unsigned)(pl.n_tail * (pl.n_chunks - 1)), st);
+                                       (unsigned)(pl.n_tail * (pl.n_chunks - 1)), st, false);
+    if (e != cudaSuccess) return fail(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
+    e = mamba_scan::launch_carry_kernel(p, st);
     if (e != cudaSuccess) return fail(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
   }
   e = mamba_scan::launch_scan_kernel(variant, mamba_scan::kLaunchEmit, tma, p, maps,
-                                     (unsigned)(pl.n_full + pl.n_tail * pl.n_chunks), st);
+                                     (unsigned)(pl.n_full + pl.n_tail * pl.n_chunks), st, split);
   if (e != cudaSuccess) return fail(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
   return MAMBA_SCAN_OK;
 }

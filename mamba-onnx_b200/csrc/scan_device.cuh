@@ -15,6 +15,7 @@ constexpr int kN = 16;     // d_state; the reference kernels support only 16 (cc
 constexpr int kRows = 32;  // (b, d) rows per CTA: one warp, one row per lane
 constexpr int kT = 16;     // time steps per tile: 64-byte rows in shared memory
 constexpr int kStages = 3;  // tiles in the shared-memory ring
+constexpr int kCarryThreads = 256;  // threads per CTA of the carry kernel
 
 enum Variant { kLinear = 0, kExact = 1, kFused = 2, kFusedExact = 3 };
 enum Mode { kEmit = 0, kAggregate = 1 };
@@ -120,6 +121,16 @@ template <int N> __device__ __forceinline__ void bulk_wait_all() {
   asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// Programmatic dependent launch: let the next grid in the stream be
+// scheduled now (it still orders itself with pdl_wait) ...
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ... and wait until the previous grid in the stream has finished and its
+// writes are visible (returns at once when this grid was launched normally).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -176,6 +187,26 @@ __device__ __forceinline__ float softplus(float x, float bias, float bias_l2e) {
 template <bool kExactMath> __device__ __forceinline__ float silu(float x) {
   if (kExactMath) return x / (1.f + expf(-x));
   return x * rcp_approx(1.f + ex2_approx(x * -1.4426950408889634f));
+}
+
+// Two consecutive steps at once: the FMA/add/multiply parts of softplus and
+// silu run as packed fp32x2 operations (each lane of the pair rounds exactly
+// like the scalar forms above); the SFU calls stay scalar.
+template <bool kExactMath>
+__device__ __forceinline__ float2 softplus2(float2 x, float bias, float2 bias_l2e) {
+  if (kExactMath) return make_float2(softplus<true>(x.x, bias, 0.f), softplus<true>(x.y, bias, 0.f));
+  const float2 s = fma2(x, make_float2(1.4426950408889634f, 1.4426950408889634f), bias_l2e);
+  float2 l = add2(make_float2(1.f, 1.f), make_float2(ex2_approx(s.x), ex2_approx(s.y)));
+  l = make_float2(s.x > 28.853900817779268f ? s.x : lg2_approx(l.x),
+                  s.y > 28.853900817779268f ? s.y : lg2_approx(l.y));
+  return mul2(l, make_float2(0.6931471805599453f, 0.6931471805599453f));
+}
+
+template <bool kExactMath> __device__ __forceinline__ float2 silu2(float2 x) {
+  if (kExactMath) return make_float2(silu<true>(x.x), silu<true>(x.y));
+  const float2 t = mul2(x, make_float2(-1.4426950408889634f, -1.4426950408889634f));
+  const float2 d = add2(make_float2(1.f, 1.f), make_float2(ex2_approx(t.x), ex2_approx(t.y)));
+  return mul2(x, make_float2(rcp_approx(d.x), rcp_approx(d.y)));
 }
 
 // Offset (in floats) of element (row, t) of a [kRows][kT] tile stored with the

@@ -10,16 +10,19 @@
 //   contraction over d_state is a register reduction with no shuffles;
 // * the sequence is streamed in tiles of 16 steps. u/delta/z tiles
 //   ([32 rows][16 steps], L contiguous) and B/C tiles ([16 steps][16 states])
-//   are fetched by TMA into a 2-stage shared-memory ring (mbarrier
+//   are fetched by TMA into a 3-stage shared-memory ring (mbarrier
 //   completion), read back as float4 through the 64-byte swizzle so the
 //   per-row reads are bank-conflict free, and B/C values are warp-wide
-//   broadcasts; outputs go through a swizzled shared tile and a TMA store;
+//   broadcasts; outputs are written over the tile's u values and leave by a
+//   TMA store, and the stage is refilled once that store has read it;
 // * the per-state update runs on packed fp32x2 FMAs (FFMA2);
 // * long sequences with few rows are split into chunks: an aggregate pass
 //   computes, per (row, chunk), the chunk's end state from zero and its decay
-//   prod(abar) (exp(A*sum(delta)) for the exact variants); the emit pass
-//   folds the aggregates of the earlier chunks into its carry-in,
-//   h_in = P*h_in + h_end, and re-runs its chunk from there.
+//   prod(abar) (exp(A*sum(delta)) for the exact variants); a carry kernel
+//   folds them in order into the state entering each chunk,
+//   h_in = P*h_in + h_end; the emit pass re-runs each chunk from its h_in.
+//   Carry and emit are programmatic dependent launches: the emit pass's
+//   whole row tiles start while the aggregate pass still runs.
 //
 // A plain-load tile path (no TMA) covers inputs that TMA cannot describe
 // (seqlen not a multiple of 4, or pointers not 16-byte aligned); it uses the
@@ -41,10 +44,66 @@ constexpr int kAcc = MAMBA_SCAN_ACC;
 
 // --------------------------------------------------------------- tile math
 
+// abar and B*delta*u of one step, for the lane's 16 states.
+template <int V>
+__device__ __forceinline__ void step_prep(const float* __restrict__ Bt_, float dt, float du,
+                                          const float2 (&Ar)[8], float2 (&a)[8], float2 (&bu)[8]) {
+  using Tr = VariantTraits<V>;
+  const float2 one2 = make_float2(1.f, 1.f);
+  const float2 dt2 = make_float2(dt, dt);
+  const float2 du2 = make_float2(du, du);
+  const float4* Bt = reinterpret_cast<const float4*>(Bt_);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float4 bq = Bt[q];
+    if (Tr::exact) {
+      // abar = exp(delta*A) = 2^(delta * A*log2(e)); Ar holds A*log2(e)
+      const float2 x0 = mul2(dt2, Ar[2 * q]);
+      const float2 x1 = mul2(dt2, Ar[2 * q + 1]);
+      a[2 * q] = make_float2(ex2_approx(x0.x), ex2_approx(x0.y));
+      a[2 * q + 1] = make_float2(ex2_approx(x1.x), ex2_approx(x1.y));
+    } else {
+      // abar = 1 + delta*A (cc:275-282 written as (1+dA)h + dBu)
+      a[2 * q] = fma2(dt2, Ar[2 * q], one2);
+      a[2 * q + 1] = fma2(dt2, Ar[2 * q + 1], one2);
+    }
+    bu[2 * q] = mul2(du2, make_float2(bq.x, bq.y));
+    bu[2 * q + 1] = mul2(du2, make_float2(bq.z, bq.w));
+  }
+}
+
+// sum_n C[n]*h[n] (cc:285-296) as two partial sums (x, y lanes of a pair).
+__device__ __forceinline__ float2 contract(const float* __restrict__ Ct_, const float2 (&h)[8]) {
+  const float4* Ct = reinterpret_cast<const float4*>(Ct_);
+  float2 acc[kAcc];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float4 cq = Ct[q];
+    const int i0 = (2 * q) % kAcc, i1 = (2 * q + 1) % kAcc;
+    if (2 * q < kAcc) acc[i0] = mul2(make_float2(cq.x, cq.y), h[2 * q]);
+    else acc[i0] = fma2(make_float2(cq.x, cq.y), h[2 * q], acc[i0]);
+    if (2 * q + 1 < kAcc) acc[i1] = mul2(make_float2(cq.z, cq.w), h[2 * q + 1]);
+    else acc[i1] = fma2(make_float2(cq.z, cq.w), h[2 * q + 1], acc[i1]);
+  }
+#pragma unroll
+  for (int w = kAcc / 2; w >= 1; w /= 2)
+#pragma unroll
+    for (int i = 0; i < w; ++i) acc[i] = add2(acc[i], acc[i + w]);
+  return acc[0];
+}
+
 // One 16-step tile for the calling lane's row. Reads the swizzled u/delta/z
 // tiles and the B/C tiles, updates h (and the decay product P, or the delta
 // sum S, in aggregate mode) and, in emit mode, writes y into the swizzled
-// output tile `os`. kPartial masks steps >= n_valid (the ragged last tile).
+// output tile `os` (which may be the u tile itself: every u value is read
+// before the first output is written). kPartial masks steps >= n_valid (the
+// ragged last tile).
+//
+// The per-step scalar work (softplus, delta*u, the silu gate, D*u) is done
+// first for all 16 steps, on packed pairs of consecutive steps. The state
+// loop then computes abar and B*delta*u of step t+1 before the C.h
+// contraction of step t, so the contraction overlaps the next step's
+// independent work.
 template <int V, int M, bool kPartial>
 __device__ __forceinline__ void compute_tile(const float* us,
                                              const float* __restrict__ ds,
@@ -55,90 +114,76 @@ __device__ __forceinline__ void compute_tile(const float* us,
                                              const float2 (&Ar)[8], float dskip, float bias,
                                              float bias_l2e, int n_valid) {
   using Tr = VariantTraits<V>;
-  const float2 one2 = make_float2(1.f, 1.f);
+  const float2 bias_l2e2 = make_float2(bias_l2e, bias_l2e);
+  const float2 dskip2 = make_float2(dskip, dskip);
+  float2 uu[8], dt[8], du[8], gate[8];
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
     const int off = row * kT + (((c ^ (row >> 1)) & 3) << 2);
     const float4 u4 = *reinterpret_cast<const float4*>(us + off);
     const float4 d4 = *reinterpret_cast<const float4*>(ds + off);
-    float uu[4] = {u4.x, u4.y, u4.z, u4.w};
-    float dd[4] = {d4.x, d4.y, d4.z, d4.w};
-    float gate[4] = {1.f, 1.f, 1.f, 1.f};
+    uu[2 * c] = make_float2(u4.x, u4.y);
+    uu[2 * c + 1] = make_float2(u4.z, u4.w);
+    dt[2 * c] = make_float2(d4.x, d4.y);
+    dt[2 * c + 1] = make_float2(d4.z, d4.w);
     if (Tr::fused) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) dd[j] = softplus<Tr::exact>(dd[j], bias, bias_l2e);
+      dt[2 * c] = softplus2<Tr::exact>(dt[2 * c], bias, bias_l2e2);
+      dt[2 * c + 1] = softplus2<Tr::exact>(dt[2 * c + 1], bias, bias_l2e2);
       if (M == kEmit) {
         const float4 z4 = *reinterpret_cast<const float4*>(zs + off);
-        gate[0] = silu<Tr::exact>(z4.x);
-        gate[1] = silu<Tr::exact>(z4.y);
-        gate[2] = silu<Tr::exact>(z4.z);
-        gate[3] = silu<Tr::exact>(z4.w);
+        gate[2 * c] = silu2<Tr::exact>(make_float2(z4.x, z4.y));
+        gate[2 * c + 1] = silu2<Tr::exact>(make_float2(z4.z, z4.w));
       }
     }
-    if (kPartial) {
+  }
+  if (kPartial) {
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-        if (4 * c + j >= n_valid) dd[j] = 0.f;  // abar = 1, input term 0: h is held
+    for (int k = 0; k < 8; ++k) {
+      if (2 * k >= n_valid) dt[k].x = 0.f;
+      if (2 * k + 1 >= n_valid) dt[k].y = 0.f;
     }
-    float yy[4];
+  }
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int t = 4 * c + j;
-      const float dt = dd[j];
-      const float du = dt * uu[j];
-      const float2 dt2 = make_float2(dt, dt);
-      const float2 du2 = make_float2(du, du);
-      const float4* Bt = reinterpret_cast<const float4*>(Bs + t * kN);
-      const float4* Ct = reinterpret_cast<const float4*>(Cs + t * kN);
-      float2 a[8], bu[8];
+  for (int k = 0; k < 8; ++k) du[k] = mul2(dt[k], uu[k]);
+  float2 a[8], bu[8];
+  step_prep<V>(Bs, dt[0].x, du[0].x, Ar, a, bu);
+  float2 s_prev = make_float2(0.f, 0.f);
+  float2 yy[8];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float4 bq = Bt[q];
-        if (Tr::exact) {
-          // abar = exp(delta*A) = 2^(delta * A*log2(e)); Ar holds A*log2(e)
-          const float2 x0 = mul2(dt2, Ar[2 * q]);
-          const float2 x1 = mul2(dt2, Ar[2 * q + 1]);
-          a[2 * q] = make_float2(ex2_approx(x0.x), ex2_approx(x0.y));
-          a[2 * q + 1] = make_float2(ex2_approx(x1.x), ex2_approx(x1.y));
-        } else {
-          // abar = 1 + delta*A (cc:275-282 written as (1+dA)h + dBu)
-          a[2 * q] = fma2(dt2, Ar[2 * q], one2);
-          a[2 * q + 1] = fma2(dt2, Ar[2 * q + 1], one2);
-        }
-        bu[2 * q] = mul2(du2, make_float2(bq.x, bq.y));
-        bu[2 * q + 1] = mul2(du2, make_float2(bq.z, bq.w));
-      }
+  for (int t = 0; t < kT; ++t) {
 #pragma unroll
-      for (int n = 0; n < 8; ++n) h[n] = fma2(a[n], h[n], bu[n]);
-      if (M == kAggregate) {
-        if (!Tr::exact) {
+    for (int n = 0; n < 8; ++n) h[n] = fma2(a[n], h[n], bu[n]);
+    if (M == kAggregate) {
+      if (!Tr::exact) {
 #pragma unroll
-          for (int n = 0; n < 8; ++n) P[n] = mul2(P[n], a[n]);
-        } else {
-          S += dt;
-        }
-        yy[j] = 0.f;
+        for (int n = 0; n < 8; ++n) P[n] = mul2(P[n], a[n]);
       } else {
-        float2 acc[kAcc];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float4 cq = Ct[q];
-          const int i0 = (2 * q) % kAcc, i1 = (2 * q + 1) % kAcc;
-          if (2 * q < kAcc) acc[i0] = mul2(make_float2(cq.x, cq.y), h[2 * q]);
-          else acc[i0] = fma2(make_float2(cq.x, cq.y), h[2 * q], acc[i0]);
-          if (2 * q + 1 < kAcc) acc[i1] = mul2(make_float2(cq.z, cq.w), h[2 * q + 1]);
-          else acc[i1] = fma2(make_float2(cq.z, cq.w), h[2 * q + 1], acc[i1]);
-        }
-#pragma unroll
-        for (int w = kAcc / 2; w >= 1; w /= 2)
-#pragma unroll
-          for (int i = 0; i < w; ++i) acc[i] = add2(acc[i], acc[i + w]);
-        float y = acc[0].x + acc[0].y;                  // sum_n C*h (cc:285-296)
-        y = fmaf(dskip, uu[j], y);                      // + D*u (cc:297)
-        yy[j] = Tr::fused ? y * gate[j] : y;            // * silu(z) (cc:300-302)
+        S += (t & 1) ? dt[t >> 1].y : dt[t >> 1].x;
       }
     }
-    if (M == kEmit) *reinterpret_cast<float4*>(os + off) = make_float4(yy[0], yy[1], yy[2], yy[3]);
+    if (t + 1 < kT) {
+      const int k = (t + 1) >> 1;
+      step_prep<V>(Bs + (t + 1) * kN, ((t + 1) & 1) ? dt[k].y : dt[k].x,
+                   ((t + 1) & 1) ? du[k].y : du[k].x, Ar, a, bu);
+    }
+    if (M == kEmit) {
+      const float2 s = contract(Cs + t * kN, h);
+      if (t & 1) {
+        float2 y = make_float2(s_prev.x + s_prev.y, s.x + s.y);
+        y = fma2(dskip2, uu[t >> 1], y);                      // + D*u (cc:297)
+        yy[t >> 1] = Tr::fused ? mul2(y, gate[t >> 1]) : y;   // * silu(z) (cc:300-302)
+      } else {
+        s_prev = s;
+      }
+    }
+  }
+  if (M == kEmit) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int off = row * kT + (((c ^ (row >> 1)) & 3) << 2);
+      *reinterpret_cast<float4*>(os + off) =
+          make_float4(yy[2 * c].x, yy[2 * c].y, yy[2 * c + 1].x, yy[2 * c + 1].y);
+    }
   }
 }
 
@@ -199,6 +244,9 @@ __global__ void __launch_bounds__(kRows, MAMBA_SCAN_MIN_BLOCKS)
     scan_kernel(const ScanParams p, const __grid_constant__ TmaMaps maps) {
   using Tr = VariantTraits<V>;
   __shared__ TileSmem sm;
+  // The carry kernel (launched next, programmatic dependent launch) may be
+  // scheduled right away; it waits for this grid to finish before reading.
+  if (M == kAggregate) pdl_trigger();
 
   const int lane = threadIdx.x;
   // Which row tile and which part of the sequence this CTA owns.
@@ -243,8 +291,8 @@ __global__ void __launch_bounds__(kRows, MAMBA_SCAN_MIN_BLOCKS)
   const float bias = (Tr::fused && p.delta_bias != nullptr) ? __ldg(p.delta_bias + dc) : 0.f;
   const float bias_l2e = bias * 1.4426950408889634f;
 
-  // Initial state: zeros (cc:241-242) or h0; emit chunks > 0 fold in the
-  // aggregates of the chunks before them.
+  // Initial state: zeros (cc:241-242) or h0; emit chunks > 0 start from the
+  // carry-in state of the chunks before them.
   float2 h[8], P[8];
   float S = 0.f;
 #pragma unroll
@@ -253,22 +301,23 @@ __global__ void __launch_bounds__(kRows, MAMBA_SCAN_MIN_BLOCKS)
     P[n] = make_float2(1.f, 1.f);
   }
   if (M == kEmit) {
-    if (p.h0 != nullptr) {
+    if (chunk > 0) {
+      // The state entering this chunk, folded by carry_kernel (launched
+      // between the two passes; wait for it and, through it, the aggregate
+      // pass). Whole row tiles and first chunks do not wait.
+      pdl_wait();
+      const float4* w = reinterpret_cast<const float4*>(
+          p.ws + (ws_row * (int64_t)(n_chunks - 1) + chunk - 1) * 2 * kN);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 e = __ldcg(w + q);
+        h[2 * q] = make_float2(e.x, e.y);
+        h[2 * q + 1] = make_float2(e.z, e.w);
+      }
+    } else if (p.h0 != nullptr) {
 #pragma unroll
       for (int n = 0; n < 8; ++n)
         h[n] = make_float2(__ldg(p.h0 + row * kN + 2 * n), __ldg(p.h0 + row * kN + 2 * n + 1));
-    }
-    if (chunk > 0) {
-      const float* w = p.ws + ws_row * (int64_t)(n_chunks - 1) * 2 * kN;
-      for (int cc = 0; cc < chunk; ++cc) {
-#pragma unroll
-        for (int n = 0; n < 8; ++n) {
-          const float2 he = make_float2(w[cc * 2 * kN + 2 * n], w[cc * 2 * kN + 2 * n + 1]);
-          const float2 pe =
-              make_float2(w[cc * 2 * kN + kN + 2 * n], w[cc * 2 * kN + kN + 2 * n + 1]);
-          h[n] = fma2(pe, h[n], he);
-        }
-      }
     }
   }
 
@@ -378,36 +427,97 @@ __global__ void __launch_bounds__(kRows, MAMBA_SCAN_MIN_BLOCKS)
   }
 }
 
+// ------------------------------------------------------------ carry kernel
+
+// Turns the chunk aggregates of the split row tiles into the states entering
+// each chunk: h_in(0) = h0 (or 0) and h_in(c) = P(c-1) * h_in(c-1) +
+// h_end(c-1), folded over the chunks in order. One thread per (row, state);
+// h_in(c) overwrites h_end(c-1) in the workspace, where the emit pass of
+// chunk c reads it. Launched after the aggregate pass as a programmatic
+// dependent launch: it lets the emit pass be scheduled at once, then waits
+// for the aggregate pass.
+__global__ void __launch_bounds__(kCarryThreads) carry_kernel(const ScanParams p) {
+  pdl_trigger();
+  const int64_t gid = (int64_t)blockIdx.x * kCarryThreads + threadIdx.x;
+  const int s = (int)(gid % kN);
+  const int64_t ws_row = gid / kN;
+  if (ws_row >= (int64_t)p.n_tail * kRows) return;
+  const int rt = p.n_full + (int)(ws_row / kRows);
+  const int b = rt / p.tiles_per_batch;
+  const int64_t d = (int64_t)(rt - b * p.tiles_per_batch) * kRows + ws_row % kRows;
+  if (d >= p.dim) return;  // padding rows of the last tile: nothing to carry
+  float h = (p.h0 != nullptr) ? __ldg(p.h0 + ((int64_t)b * p.dim + d) * kN + s) : 0.f;
+  pdl_wait();
+  const int n = p.n_chunks - 1;
+  float* w = p.ws + ws_row * (int64_t)n * 2 * kN + s;
+  constexpr int kAhead = 8;  // chunks whose loads are in flight together
+  int c = 0;
+  for (; c + kAhead <= n; c += kAhead) {
+    float he[kAhead], pe[kAhead];
+#pragma unroll
+    for (int f = 0; f < kAhead; ++f) {
+      he[f] = __ldcg(w + (c + f) * 2 * kN);
+      pe[f] = __ldcg(w + (c + f) * 2 * kN + kN);
+    }
+#pragma unroll
+    for (int f = 0; f < kAhead; ++f) {
+      h = fmaf(pe[f], h, he[f]);
+      w[(c + f) * 2 * kN] = h;
+    }
+  }
+  for (; c < n; ++c) {
+    h = fmaf(__ldcg(w + c * 2 * kN + kN), h, __ldcg(w + c * 2 * kN));
+    w[c * 2 * kN] = h;
+  }
+}
+
 // ------------------------------------------------------------------ launch
+
+// Launch `kernel` on `st`; with `pdl` as a programmatic dependent launch (the
+// grid may start before the previous kernel in the stream has finished; it
+// orders itself with griddepcontrol.wait).
+template <typename... Args>
+static cudaError_t launch(void (*kernel)(Args...), unsigned blocks, unsigned threads,
+                          cudaStream_t st, bool pdl, const Args&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(blocks);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
 
 template <int V>
 static cudaError_t launch_v(int mode, bool tma, const ScanParams& p, const TmaMaps& maps,
-                            unsigned blocks, cudaStream_t st) {
-  const dim3 grid(blocks);
-  const dim3 block(kRows);
-  if (mode == kLaunchEmit) {
-    if (tma)
-      scan_kernel<V, kEmit, true><<<grid, block, 0, st>>>(p, maps);
-    else
-      scan_kernel<V, kEmit, false><<<grid, block, 0, st>>>(p, maps);
-  } else {
-    if (tma)
-      scan_kernel<V, kAggregate, true><<<grid, block, 0, st>>>(p, maps);
-    else
-      scan_kernel<V, kAggregate, false><<<grid, block, 0, st>>>(p, maps);
-  }
-  return cudaGetLastError();
+                            unsigned blocks, cudaStream_t st, bool pdl) {
+  if (mode == kLaunchEmit)
+    return tma ? launch(scan_kernel<V, kEmit, true>, blocks, kRows, st, pdl, p, maps)
+               : launch(scan_kernel<V, kEmit, false>, blocks, kRows, st, pdl, p, maps);
+  return tma ? launch(scan_kernel<V, kAggregate, true>, blocks, kRows, st, pdl, p, maps)
+             : launch(scan_kernel<V, kAggregate, false>, blocks, kRows, st, pdl, p, maps);
 }
 
 cudaError_t launch_scan_kernel(int variant, int mode, bool tma, const ScanParams& p,
-                               const TmaMaps& maps, unsigned grid, cudaStream_t stream) {
+                               const TmaMaps& maps, unsigned grid, cudaStream_t stream,
+                               bool pdl) {
   switch (variant) {
-    case kLinear: return launch_v<kLinear>(mode, tma, p, maps, grid, stream);
-    case kExact: return launch_v<kExact>(mode, tma, p, maps, grid, stream);
-    case kFused: return launch_v<kFused>(mode, tma, p, maps, grid, stream);
-    case kFusedExact: return launch_v<kFusedExact>(mode, tma, p, maps, grid, stream);
+    case kLinear: return launch_v<kLinear>(mode, tma, p, maps, grid, stream, pdl);
+    case kExact: return launch_v<kExact>(mode, tma, p, maps, grid, stream, pdl);
+    case kFused: return launch_v<kFused>(mode, tma, p, maps, grid, stream, pdl);
+    case kFusedExact: return launch_v<kFusedExact>(mode, tma, p, maps, grid, stream, pdl);
     default: return cudaErrorInvalidValue;
   }
+}
+
+cudaError_t launch_carry_kernel(const ScanParams& p, cudaStream_t stream) {
+  const int64_t threads = (int64_t)p.n_tail * kRows * kN;
+  const unsigned blocks = (unsigned)((threads + kCarryThreads - 1) / kCarryThreads);
+  return launch(carry_kernel, blocks, kCarryThreads, stream, true, p);
 }
 
 template <int V>

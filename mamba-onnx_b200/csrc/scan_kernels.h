@@ -22,7 +22,10 @@ struct ScanParams {
   const float* h0;
   float* out;
   float* h_last;
-  float* ws;  // chunk aggregates: [n_tail*32 rows][n_chunks-1][32] (16 states, 16 decays)
+  // chunk aggregates, [n_tail*32 rows][n_chunks-1][32 floats]: the chunk's end
+  // state from zero (16) and its decay (16); the carry kernel then replaces
+  // the end state of chunk c with the state entering chunk c+1.
+  float* ws;
   int64_t batch;
   int64_t dim;
   int64_t seqlen;
@@ -30,7 +33,7 @@ struct ScanParams {
   // [0, n_full) are scanned in one pass over the whole sequence; row tiles
   // [n_full, n_full + n_tail) are split into n_chunks chunks of chunk_len
   // steps (the last chunk takes the rest) that run in parallel: an aggregate
-  // launch over chunks 0..n_chunks-2, then the emit launch.
+  // launch over chunks 0..n_chunks-2, the carry kernel, then the emit launch.
   int64_t chunk_len;    // multiple of 32
   int tiles_per_batch;  // ceil(dim / 32)
   int n_full;
@@ -48,9 +51,15 @@ enum LaunchMode { kLaunchEmit = 0, kLaunchAggregate = 1 };
 
 // Enqueue one scan kernel (variant 0..3, mode, TMA or plain-load tile path)
 // on `stream` with a 1-D grid of `blocks` CTAs: n_full + n_tail * n_chunks
-// for emit, n_tail * (n_chunks - 1) for aggregate.
+// for emit, n_tail * (n_chunks - 1) for aggregate. `pdl`: programmatic
+// dependent launch (the emit pass after the carry kernel).
 cudaError_t launch_scan_kernel(int variant, int mode, bool tma, const ScanParams& p,
-                               const TmaMaps& maps, unsigned blocks, cudaStream_t stream);
+                               const TmaMaps& maps, unsigned blocks, cudaStream_t stream,
+                               bool pdl);
+
+// Enqueue the carry kernel (between the aggregate and emit passes of a split
+// plan), as a programmatic dependent launch.
+cudaError_t launch_carry_kernel(const ScanParams& p, cudaStream_t stream);
 
 // Resident CTAs per SM of one kernel instantiation (occupancy calculator).
 cudaError_t max_blocks_per_sm(int variant, int mode, bool tma, int* blocks);
