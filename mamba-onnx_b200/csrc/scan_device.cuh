@@ -171,10 +171,13 @@ __device__ __forceinline__ float rcp_approx(float x) {
 template <bool kExactMath>
 __device__ __forceinline__ float softplus(float x, float bias, float bias_l2e) {
   if (kExactMath) {
+    // Both candidates are computed and one is selected (no divergent
+    // branches, so the steps of a tile can be interleaved); for x > 88.7,
+    // e = inf and l = inf are computed but not selected.
     x += bias;
-    if (x > 20.f) return x;
-    if (x < -20.f) return expf(x);
-    return log1pf(expf(x));
+    const float e = expf(x);
+    const float l = log1pf(e);
+    return x > 20.f ? x : (x < -20.f ? e : l);
   } else {
     const float s = fmaf(x, 1.4426950408889634f, bias_l2e);
     const float l = lg2_approx(1.f + ex2_approx(s));
