@@ -264,7 +264,8 @@ def main():
     stream = torch.cuda.current_stream(device)
     ws_bytes = cuda.workspace_size(OP, BATCH, DIM, SEQLEN)
     ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=device)
-    launches_per_step = 1 if ws_bytes == 0 else 2
+    # one emit launch, or aggregate + carry + emit when the plan splits sequences
+    launches_per_step = 1 if ws_bytes == 0 else 3
 
     def step():
         cuda.selective_scan(OP, u, delta, A, Bm, Cm, Dv, z, out=out, workspace=ws, stream=stream)
@@ -324,7 +325,7 @@ def main():
             "gpu_launches": launches_per_step * args.steps,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                          "frac": achieved / hbm_peak, "traffic": traffic,
-                         "per": "op call (aggregate + emit launches when the plan splits)",
+                         "per": "op call (aggregate + carry + emit launches when the plan splits)",
                          "peak_source": f"{peak_kind} hbm_gbs",
                          "algorithmic_bytes_per_launch": algo,
                          "sfu_ops_per_launch": sfu_ops(BATCH, DIM, SEQLEN)},

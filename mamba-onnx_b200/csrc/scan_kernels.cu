@@ -414,15 +414,17 @@ __global__ void __launch_bounds__(kRows, MAMBA_SCAN_MIN_BLOCKS)
       }
     }
   } else {
-    float* w = p.ws + (ws_row * (int64_t)(n_chunks - 1) + chunk) * 2 * kN;
+    // 32 floats per (row, chunk): the end state, then the decay.
+    float4* w = reinterpret_cast<float4*>(p.ws + (ws_row * (int64_t)(n_chunks - 1) + chunk) * 2 * kN);
 #pragma unroll
-    for (int n = 0; n < 8; ++n) {
-      float2 pn = P[n];
-      if (Tr::exact) pn = make_float2(ex2_approx(Ar[n].x * S), ex2_approx(Ar[n].y * S));
-      w[2 * n] = h[n].x;
-      w[2 * n + 1] = h[n].y;
-      w[kN + 2 * n] = pn.x;
-      w[kN + 2 * n + 1] = pn.y;
+    for (int q = 0; q < 4; ++q) {
+      float2 p0 = P[2 * q], p1 = P[2 * q + 1];
+      if (Tr::exact) {
+        p0 = make_float2(ex2_approx(Ar[2 * q].x * S), ex2_approx(Ar[2 * q].y * S));
+        p1 = make_float2(ex2_approx(Ar[2 * q + 1].x * S), ex2_approx(Ar[2 * q + 1].y * S));
+      }
+      w[q] = make_float4(h[2 * q].x, h[2 * q].y, h[2 * q + 1].x, h[2 * q + 1].y);
+      w[4 + q] = make_float4(p0.x, p0.y, p1.x, p1.y);
     }
   }
 }
@@ -451,23 +453,24 @@ __global__ void __launch_bounds__(kCarryThreads) carry_kernel(const ScanParams p
   const int n = p.n_chunks - 1;
   float* w = p.ws + ws_row * (int64_t)n * 2 * kN + s;
   constexpr int kAhead = 8;  // chunks whose loads are in flight together
-  int c = 0;
-  for (; c + kAhead <= n; c += kAhead) {
+  for (int c = 0; c < n; c += kAhead) {
     float he[kAhead], pe[kAhead];
 #pragma unroll
     for (int f = 0; f < kAhead; ++f) {
-      he[f] = __ldcg(w + (c + f) * 2 * kN);
-      pe[f] = __ldcg(w + (c + f) * 2 * kN + kN);
+      he[f] = 0.f;
+      pe[f] = 1.f;
+      if (c + f < n) {
+        he[f] = __ldcg(w + (c + f) * 2 * kN);
+        pe[f] = __ldcg(w + (c + f) * 2 * kN + kN);
+      }
     }
 #pragma unroll
     for (int f = 0; f < kAhead; ++f) {
-      h = fmaf(pe[f], h, he[f]);
-      w[(c + f) * 2 * kN] = h;
+      if (c + f < n) {
+        h = fmaf(pe[f], h, he[f]);
+        w[(c + f) * 2 * kN] = h;
+      }
     }
-  }
-  for (; c < n; ++c) {
-    h = fmaf(__ldcg(w + c * 2 * kN + kN), h, __ldcg(w + c * 2 * kN));
-    w[c * 2 * kN] = h;
   }
 }
 
