@@ -18,6 +18,15 @@ roofline  — the scan kernel's algorithmic HBM bytes per launch / its launch
 cpu_baseline — the reference's own C++ plugin (oracle/_ref, OpenMP, all host
             threads) on a sample of the same workload.
 --impl reference runs that reference plugin alone, as the reference arm.
+
+    python bench.py --workload mamba130m [--gpus N] [--steps K] [--warmup W]
+
+Mamba-130m forward (24 blocks, fp32) at batch 1 x seqlen 1024 per GPU with
+every selective scan on SelectiveScanFusedExact; one step = one CUDA-graph
+replay of the forward; value in tokens/s (all ranks; each rank runs its own
+replica, no collective). Its cpu_baseline (and --impl reference) is the same
+forward on the host: torch CPU GEMMs with the reference's C++ plugin doing
+the scans.
 """
 from __future__ import annotations
 
@@ -226,8 +235,11 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ncu-case", action="store_true",
                     help="for profilers: build the inputs, run warmup+steps calls, print nothing timed")
+    ap.add_argument("--workload", choices=["scan", "mamba130m"], default="scan")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
+    if args.workload == "mamba130m":
+        return run_model(args)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -398,6 +410,212 @@ def end_to_end(torch, cuda, device, args, world):
     return {"value": world * B * D * L * NSTATE / (ms * 1e-3), "unit": UNIT,
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": ms,
             "steps": n, "pipeline": "per batch entry on 2 streams, pinned host buffers"}
+
+
+# ---------------------------------------------------------------- Mamba-130m forward
+
+MODEL_BATCH, MODEL_SEQLEN = 1, 1024
+MODEL_METRIC, MODEL_UNIT = "Mamba-130m forward tokens/s", "tokens/s"
+MODEL_WORKLOAD = ("Mamba-130m forward (24 blocks, d_model 768, d_inner 1536, d_state 16, "
+                  "vocab 50280), fp32, batch 1 x seqlen 1024 per GPU, every selective scan on "
+                  "SelectiveScanFusedExact")
+
+
+def model_cpu_sample(n_threads, budget_s=30.0):
+    """The same forward on the host: torch CPU GEMMs, the reference C++ plugin
+    (oracle/_ref, OpenMP) for each layer's scan; delta_bias is added to delta
+    before the plugin call (the plugin has no bias input)."""
+    import torch
+
+    from mamba_onnx.model import MambaLM, mamba_130m
+    from oracle import oracle
+
+    torch.set_num_threads(n_threads)
+    model = MambaLM(mamba_130m()).init_random(0)
+    ids = torch.randint(0, model.cfg.vocab_size, (MODEL_BATCH, MODEL_SEQLEN),
+                        generator=torch.Generator().manual_seed(SEED))
+    kind = "reference" if oracle.ref_available() else "port"
+
+    def host_scan(op, u, delta, A, B, C, D, z, delta_bias=None, h0=None, h_last=None):
+        if delta_bias is not None:
+            delta = delta + delta_bias[None, :, None]
+        arrs = [t.detach().contiguous().numpy() for t in (u, delta, A, B, C, D, z)]
+        if kind == "reference":
+            out = oracle.ref_run(op, *arrs, n_threads=n_threads)
+        else:
+            out = oracle.scan_f32ref(op, *arrs)
+        return torch.from_numpy(out)
+
+    model(ids[:, :64], scan=host_scan)  # warm-up (thread pools, page-in)
+    times = []
+    while not times or (sum(times) < budget_s and len(times) < 3):
+        t0 = time.perf_counter()
+        model(ids, scan=host_scan)
+        times.append(time.perf_counter() - t0)
+    tokens = MODEL_BATCH * MODEL_SEQLEN
+    return {"value": tokens / statistics.median(times), "unit": MODEL_UNIT, "cores": n_threads,
+            "kind": kind,
+            "sample": f"the full forward (batch {MODEL_BATCH} x {MODEL_SEQLEN}), median of "
+                      f"{len(times)} runs after a 64-token warm-up; torch CPU GEMMs and the "
+                      f"reference plugin's scans on {n_threads} threads"}
+
+
+def run_model(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        from oracle import oracle
+
+        cpu = model_cpu_sample(oracle.host_threads())
+        print(json.dumps({
+            "impl": "reference", "metric": MODEL_METRIC, "value": cpu["value"],
+            "unit": MODEL_UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1e3 * MODEL_SEQLEN / cpu["value"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (random init, Mamba's initialisation)",
+            "config": {"workload": MODEL_WORKLOAD, "batch_per_gpu": MODEL_BATCH,
+                       "seqlen": MODEL_SEQLEN},
+            "cpu_baseline": cpu,
+            "e2e": {"value": cpu["value"], "unit": MODEL_UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}), flush=True)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    from mamba_onnx import cuda
+    from mamba_onnx.model import SCAN_OP, MambaLM, mamba_130m
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+
+    def max_over_ranks(ms):
+        if world == 1:
+            return ms
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import oracle
+
+        cpu = model_cpu_sample(oracle.host_threads())
+
+    B, L = MODEL_BATCH, MODEL_SEQLEN
+    model = MambaLM(mamba_130m()).init_random(0).to(device)
+    ids, logits, graph = model.capture(B, L)
+    g = torch.Generator(device=device).manual_seed(SEED + rank)
+    ids.copy_(torch.randint(0, model.cfg.vocab_size, (B, L), device=device, generator=g))
+    stream = torch.cuda.current_stream(device)
+
+    def timed(fn, n):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(n):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / n
+
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(device) as clocks:
+        ms = timed(graph.replay, args.steps)
+    if world > 1:
+        dist.barrier()
+    ms_per_step = max_over_ranks(ms)
+    value = world * B * L / (ms_per_step * 1e-3)
+
+    # end to end: token ids from pinned host memory, the last position's
+    # logits back to pinned host memory, every step
+    host_ids = ids.cpu().pin_memory()
+    host_last = torch.empty(B, model.cfg.vocab_size).pin_memory()
+
+    def e2e_step():
+        ids.copy_(host_ids, non_blocking=True)
+        graph.replay()
+        host_last.copy_(logits[:, -1], non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(timed(e2e_step, max(3, args.e2e_steps)))
+
+    # the 24 scans of one forward alone (same shapes, one CUDA graph)
+    D, N = model.cfg.d_inner, model.cfg.d_state
+    sg = torch.Generator(device=device).manual_seed(3)
+    u, z = (torch.randn(B, D, L, device=device, generator=sg) for _ in range(2))
+    delta = torch.randn(B, D, L, device=device, generator=sg) * 0.1
+    Bm, Cm = (torch.randn(B, L, N, device=device, generator=sg) for _ in range(2))
+    layer = model.layers[0]
+    A = -torch.exp(layer.A_log.detach())
+    scan_args = (SCAN_OP, u, delta, A, Bm, Cm, layer.D.detach(), z)
+    out = torch.empty_like(u)
+    ws = torch.empty(max(1, cuda.workspace_size(SCAN_OP, B, D, L)), dtype=torch.uint8,
+                     device=device)
+
+    def scans():
+        for _ in range(model.cfg.n_layer):
+            cuda.selective_scan(*scan_args, delta_bias=layer.dt_proj_bias.detach(), out=out,
+                                workspace=ws)
+
+    side = torch.cuda.Stream(device)
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        scans()
+    stream.wait_stream(side)
+    sgraph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(sgraph):
+        scans()
+    sgraph.replay()
+    torch.cuda.synchronize()
+    scan_ms = timed(sgraph.replay, 20)
+    launches_per_scan = 3 if cuda.workspace_size(SCAN_OP, B, D, L) > 0 else 1
+
+    if rank == 0:
+        hbm_peak, peak_kind = measured_peaks()
+        algo = model.cfg.n_layer * algorithmic_bytes(B, D, L)
+        achieved = algo / (scan_ms * 1e-3) / 1e9
+        line = {
+            "metric": MODEL_METRIC, "value": value, "unit": MODEL_UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (random init with Mamba's initialisation, uniform token ids)",
+            "config": {"workload": MODEL_WORKLOAD, "batch_per_gpu": B, "global_batch": B * world,
+                       "seqlen": L, "parallelism": f"replica per GPU x{world}, no collective",
+                       "step": "one CUDA-graph replay of the forward",
+                       "l2": "weights 0.52 GB > L2; no flush"},
+            "e2e": {"value": world * B * L / (e2e_ms * 1e-3), "unit": MODEL_UNIT,
+                    "h2d_bytes_per_step": host_ids.numel() * 8,
+                    "d2h_bytes_per_step": host_last.numel() * 4, "ms_per_step": e2e_ms,
+                    "path": "pinned token ids -> graph replay -> last-position logits to host"},
+            "gpu_launches": launches_per_scan * model.cfg.n_layer * args.steps,
+            "scan_ms_per_step": scan_ms,
+            "roofline": {"bound": "hbm", "kernel": f"the {model.cfg.n_layer} {SCAN_OP} calls of "
+                         f"one forward (1x{D}x{L} each)", "achieved": achieved, "peak": hbm_peak,
+                         "unit": "GB/s", "frac": achieved / hbm_peak, "traffic": None,
+                         "peak_source": f"{peak_kind} hbm_gbs",
+                         "algorithmic_bytes_per_step": algo},
+            "clocks": clocks.summary(),
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        del graph, sgraph
+        dist.destroy_process_group()
 
 
 if __name__ == "__main__":

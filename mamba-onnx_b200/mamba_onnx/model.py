@@ -1,0 +1,244 @@
+"""Mamba language model whose selective scans run on the CUDA op.
+
+The reference project ships only the scan op; a Mamba graph around it is the
+caller's (its block dataflow is benchmarks/profiler.py:18-150: in_proj ->
+causal depthwise conv1d + SiLU -> x_proj -> dt_proj + softplus -> scan ->
+x SiLU(z) -> out_proj). This module is that caller, written in torch for the
+GEMMs, the convolution and the norms, with every scan sent through
+``mamba_onnx.cuda.selective_scan`` as ``SelectiveScanFusedExact`` (abar =
+exp(delta*A), softplus(delta + dt_proj.bias) fused into the op through its
+``delta_bias`` input). Parameter names and shapes follow transformers'
+``MambaForCausalLM`` so its weights load directly; its ``MambaMixer.slow_forward``
+is the numerical reference.
+
+Everything is float32. ``forward`` runs a whole sequence; ``step`` decodes one
+token from a ``DecodeState`` (the convolution window and the 16 scan states
+per channel), which the scan carries in through ``h0`` and out through
+``h_last``.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+
+from . import cuda
+
+SCAN_OP = "SelectiveScanFusedExact"
+
+
+@dataclass(frozen=True)
+class MambaConfig:
+    d_model: int = 768
+    n_layer: int = 24
+    vocab_size: int = 50280
+    d_state: int = 16
+    d_conv: int = 4
+    expand: int = 2
+    dt_rank: int = 0  # 0: ceil(d_model / 16)
+    rms_eps: float = 1e-5
+
+    @property
+    def d_inner(self) -> int:
+        return self.expand * self.d_model
+
+    @property
+    def rank(self) -> int:
+        return self.dt_rank or math.ceil(self.d_model / 16)
+
+
+def mamba_130m() -> MambaConfig:
+    """Mamba-130m: 24 blocks, d_model 768, d_inner 1536, d_state 16, dt_rank 48."""
+    return MambaConfig()
+
+
+class MambaLayer(torch.nn.Module):
+    """One residual block: x + mixer(rmsnorm(x))."""
+
+    def __init__(self, cfg: MambaConfig):
+        super().__init__()
+        d, D, N, R = cfg.d_model, cfg.d_inner, cfg.d_state, cfg.rank
+        f32 = dict(dtype=torch.float32)
+        self.cfg = cfg
+        self.norm_weight = torch.nn.Parameter(torch.ones(d, **f32))
+        self.in_proj_weight = torch.nn.Parameter(torch.empty(2 * D, d, **f32))
+        self.conv_weight = torch.nn.Parameter(torch.empty(D, 1, cfg.d_conv, **f32))
+        self.conv_bias = torch.nn.Parameter(torch.zeros(D, **f32))
+        self.x_proj_weight = torch.nn.Parameter(torch.empty(R + 2 * N, D, **f32))
+        self.dt_proj_weight = torch.nn.Parameter(torch.empty(D, R, **f32))
+        self.dt_proj_bias = torch.nn.Parameter(torch.empty(D, **f32))
+        self.A_log = torch.nn.Parameter(torch.empty(D, N, **f32))
+        self.D = torch.nn.Parameter(torch.ones(D, **f32))
+        self.out_proj_weight = torch.nn.Parameter(torch.empty(d, D, **f32))
+
+    def _norm(self, x):
+        var = x.pow(2).mean(-1, keepdim=True)
+        return x * torch.rsqrt(var + self.cfg.rms_eps) * self.norm_weight
+
+    def _ssm_inputs(self, x):
+        """x [B, D, L] after conv + SiLU -> delta [B, D, L] (before bias), B, C [B, L, N]."""
+        N, R = self.cfg.d_state, self.cfg.rank
+        x_dbl = torch.matmul(x.transpose(1, 2), self.x_proj_weight.t())  # [B, L, R + 2N]
+        delta = torch.matmul(self.dt_proj_weight, x_dbl[..., :R].transpose(1, 2))  # [B, D, L]
+        Bm = x_dbl[..., R:R + N].contiguous()
+        Cm = x_dbl[..., R + N:].contiguous()
+        return delta, Bm, Cm
+
+    def forward(self, h, A, conv_state=None, ssm_state=None, scan=None):
+        """h [B, L, d_model] -> h + mixer(norm(h)); A = -exp(A_log). Given
+        conv_state [B, D, d_conv] and ssm_state [B, D, N], they receive the
+        state after the last token (for decoding on from here). ``scan``
+        replaces the CUDA op (same signature as cuda.selective_scan)."""
+        scan = scan or cuda.selective_scan
+        D, L, K = self.cfg.d_inner, h.shape[1], self.cfg.d_conv
+        xz = torch.matmul(self.in_proj_weight, self._norm(h).transpose(1, 2))  # [B, 2D, L]
+        x = F.silu(F.conv1d(xz[:, :D], self.conv_weight, self.conv_bias,
+                            padding=K - 1, groups=D)[..., :L])
+        z = xz[:, D:].contiguous()
+        delta, Bm, Cm = self._ssm_inputs(x)
+        y = scan(SCAN_OP, x, delta, A, Bm, Cm, self.D, z, delta_bias=self.dt_proj_bias,
+                 h_last=ssm_state)
+        if conv_state is not None:  # the last K inputs of the convolution, zero-padded
+            conv_state.copy_(F.pad(xz[:, :D], (max(0, K - L), 0))[..., -K:])
+        return h + torch.matmul(y.transpose(1, 2), self.out_proj_weight.t())
+
+    def step(self, h, A, conv_state, ssm_state):
+        """One token: h [B, 1, d_model]; conv_state [B, D, d_conv] (last inputs of
+        the convolution, oldest first) and ssm_state [B, D, N] are updated."""
+        D = self.cfg.d_inner
+        xz = torch.matmul(self.in_proj_weight, self._norm(h).transpose(1, 2))  # [B, 2D, 1]
+        conv_state.copy_(torch.cat([conv_state[..., 1:], xz[:, :D]], dim=-1))
+        x = torch.sum(conv_state * self.conv_weight[:, 0, :], dim=-1) + self.conv_bias
+        x = F.silu(x).unsqueeze(-1).contiguous()  # [B, D, 1]
+        z = xz[:, D:].contiguous()
+        delta, Bm, Cm = self._ssm_inputs(x)
+        new_state = torch.empty_like(ssm_state)
+        y = cuda.selective_scan(SCAN_OP, x, delta, A, Bm, Cm, self.D, z,
+                                delta_bias=self.dt_proj_bias, h0=ssm_state, h_last=new_state)
+        ssm_state.copy_(new_state)
+        return h + torch.matmul(y.transpose(1, 2), self.out_proj_weight.t())
+
+
+@dataclass
+class DecodeState:
+    conv: list  # per layer [B, D, d_conv]
+    ssm: list   # per layer [B, D, N]
+
+
+class MambaLM(torch.nn.Module):
+    """Embedding -> n_layer MambaLayers -> RMSNorm -> tied LM head."""
+
+    def __init__(self, cfg: MambaConfig):
+        super().__init__()
+        self.cfg = cfg
+        self.embedding = torch.nn.Parameter(torch.empty(cfg.vocab_size, cfg.d_model))
+        self.layers = torch.nn.ModuleList(MambaLayer(cfg) for _ in range(cfg.n_layer))
+        self.norm_f_weight = torch.nn.Parameter(torch.ones(cfg.d_model))
+
+    # ---------------------------------------------------------------- weights
+
+    @torch.no_grad()
+    def init_random(self, seed: int = 0, dt_min: float = 1e-3, dt_max: float = 1e-1):
+        """Mamba's initialisation: A_log = log(1..N) per channel (S4D-real),
+        dt log-uniform in [dt_min, dt_max] with dt_proj.bias = softplus^-1(dt),
+        D = 1, conv and projections N(0, 0.02) (conv bias 0)."""
+        g = torch.Generator(device="cpu").manual_seed(seed)
+        cfg = self.cfg
+        normal = lambda t: t.copy_(torch.randn(t.shape, generator=g) * 0.02)  # noqa: E731
+        normal(self.embedding)
+        for layer in self.layers:
+            for w in (layer.in_proj_weight, layer.conv_weight, layer.x_proj_weight,
+                      layer.dt_proj_weight, layer.out_proj_weight):
+                normal(w)
+            layer.conv_bias.zero_()
+            layer.norm_weight.fill_(1.0)
+            dt = torch.exp(torch.rand(cfg.d_inner, generator=g)
+                           * (math.log(dt_max) - math.log(dt_min)) + math.log(dt_min))
+            layer.dt_proj_bias.copy_(dt + torch.log(-torch.expm1(-dt)))
+            layer.A_log.copy_(torch.log(torch.arange(1, cfg.d_state + 1, dtype=torch.float32))
+                              .repeat(cfg.d_inner, 1))
+            layer.D.fill_(1.0)
+        self.norm_f_weight.fill_(1.0)
+        return self
+
+    HF_NAMES = {
+        "norm_weight": "norm.weight",
+        "in_proj_weight": "mixer.in_proj.weight",
+        "conv_weight": "mixer.conv1d.weight",
+        "conv_bias": "mixer.conv1d.bias",
+        "x_proj_weight": "mixer.x_proj.weight",
+        "dt_proj_weight": "mixer.dt_proj.weight",
+        "dt_proj_bias": "mixer.dt_proj.bias",
+        "A_log": "mixer.A_log",
+        "D": "mixer.D",
+        "out_proj_weight": "mixer.out_proj.weight",
+    }
+
+    @torch.no_grad()
+    def load_hf_state_dict(self, sd: dict):
+        """Copy weights from a transformers MambaForCausalLM state dict."""
+        self.embedding.copy_(sd["backbone.embeddings.weight"])
+        self.norm_f_weight.copy_(sd["backbone.norm_f.weight"])
+        for i, layer in enumerate(self.layers):
+            for ours, theirs in self.HF_NAMES.items():
+                getattr(layer, ours).copy_(sd[f"backbone.layers.{i}.{theirs}"])
+        return self
+
+    # ---------------------------------------------------------------- forward
+
+    def _head(self, h):
+        var = h.pow(2).mean(-1, keepdim=True)
+        h = h * torch.rsqrt(var + self.cfg.rms_eps) * self.norm_f_weight
+        return torch.matmul(h, self.embedding.t())
+
+    @torch.no_grad()
+    def forward(self, input_ids, scan=None):
+        """input_ids [B, L] int64 -> logits [B, L, vocab]. ``scan`` replaces the
+        CUDA op in every layer (same signature as cuda.selective_scan); by
+        default the scans run on cuda.selective_scan and need a CUDA device."""
+        h = F.embedding(input_ids, self.embedding)
+        for layer in self.layers:
+            h = layer(h, -torch.exp(layer.A_log), scan=scan)
+        return self._head(h)
+
+    @torch.no_grad()
+    def prefill(self, input_ids):
+        """forward() that also returns the DecodeState after the last token."""
+        state = self.new_state(input_ids.shape[0])
+        h = F.embedding(input_ids, self.embedding)
+        for layer, cs, ss in zip(self.layers, state.conv, state.ssm):
+            h = layer(h, -torch.exp(layer.A_log), cs, ss)
+        return self._head(h), state
+
+    def new_state(self, batch: int) -> DecodeState:
+        cfg, dev = self.cfg, self.embedding.device
+        return DecodeState(
+            conv=[torch.zeros(batch, cfg.d_inner, cfg.d_conv, device=dev) for _ in self.layers],
+            ssm=[torch.zeros(batch, cfg.d_inner, cfg.d_state, device=dev) for _ in self.layers])
+
+    @torch.no_grad()
+    def step(self, input_ids, state: DecodeState):
+        """One decoding step: input_ids [B] -> logits [B, vocab]; state updated."""
+        h = F.embedding(input_ids[:, None], self.embedding)
+        for layer, cs, ss in zip(self.layers, state.conv, state.ssm):
+            h = layer.step(h, -torch.exp(layer.A_log), cs, ss)
+        return self._head(h)[:, 0]
+
+    @torch.no_grad()
+    def capture(self, batch: int, seqlen: int, warmup: int = 3):
+        """CUDA-graph the forward for a fixed shape. Returns (ids, logits, graph):
+        write token ids into ``ids``, ``graph.replay()``, read ``logits``."""
+        dev = self.embedding.device
+        ids = torch.zeros(batch, seqlen, dtype=torch.int64, device=dev)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                self.forward(ids)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            logits = self.forward(ids)
+        return ids, logits, graph

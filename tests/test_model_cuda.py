@@ -1,0 +1,101 @@
+"""GPU: the Mamba language model with every selective scan on the CUDA op.
+
+Oracle: transformers' MambaForCausalLM with the same weights. Without the
+mamba-ssm kernels it runs MambaMixer.slow_forward: exact discretisation
+exp(delta*A), softplus(dt_proj(x)), a sequential scan in torch. Our model
+sends the scan through SelectiveScanFusedExact with dt_proj.bias as the
+op's delta_bias.
+
+At Mamba-130m depth (24 random-initialised blocks) fp32 rounding differences
+of any origin (a different GEMM algorithm is enough) grow about 1000-fold
+from the first block to the logits, so the 130m tests use the float64 run
+of the transformers model as ground truth and require our fp32 logits to be
+no further from it than transformers' own fp32 run is (with a 3x margin).
+"""
+import warnings
+
+import pytest
+import torch
+
+from mamba_onnx.model import MambaConfig, MambaLM, mamba_130m
+
+pytestmark = pytest.mark.gpu
+
+transformers = pytest.importorskip("transformers")
+
+
+def _hf(cfg: MambaConfig, seed: int, device):
+    torch.manual_seed(seed)
+    hf_cfg = transformers.MambaConfig(vocab_size=cfg.vocab_size, hidden_size=cfg.d_model,
+                                      state_size=cfg.d_state, num_hidden_layers=cfg.n_layer,
+                                      expand=cfg.expand, conv_kernel=cfg.d_conv,
+                                      layer_norm_epsilon=cfg.rms_eps)
+    with warnings.catch_warnings():
+        warnings.simplefilter("ignore")
+        return transformers.MambaForCausalLM(hf_cfg).to(device).eval()
+
+
+def _ids(vocab, L, seed, device, batch=1):
+    g = torch.Generator(device=device).manual_seed(seed)
+    return torch.randint(0, vocab, (batch, L), device=device, generator=g)
+
+
+def _normrel(a, b):
+    return ((a.double() - b.double()).norm() / b.double().norm()).item()
+
+
+@torch.no_grad()
+def _hf_logits(hf, ids):
+    with warnings.catch_warnings():
+        warnings.simplefilter("ignore")
+        return hf(ids).logits
+
+
+def test_small_model_matches_transformers(cuda_device):
+    cfg = MambaConfig(d_model=64, n_layer=2, vocab_size=100)
+    hf = _hf(cfg, 1, cuda_device)
+    ours = MambaLM(cfg).load_hf_state_dict(hf.state_dict()).to(cuda_device)
+    for batch, L in [(1, 40), (3, 77), (2, 300)]:
+        ids = _ids(cfg.vocab_size, L, batch + L, cuda_device, batch)
+        assert _normrel(ours(ids), _hf_logits(hf, ids)) < 1e-5, (batch, L)
+
+
+@pytest.mark.parametrize("L", [64, 1024])
+def test_mamba_130m_matches_transformers_float64(cuda_device, L):
+    """L = 1024, batch 1 is the Mamba-130m forward workload (24 blocks)."""
+    cfg = mamba_130m()
+    hf = _hf(cfg, 2, cuda_device)
+    ours = MambaLM(cfg).load_hf_state_dict(hf.state_dict()).to(cuda_device)
+    ids = _ids(cfg.vocab_size, L, 7, cuda_device)
+    got = ours(ids)
+    ref32 = _hf_logits(hf, ids)
+    ref64 = _hf_logits(hf.double(), ids)
+    e_ours, e_hf32 = _normrel(got, ref64), _normrel(ref32, ref64)
+    assert e_ours <= 3 * e_hf32 + 1e-6, (e_ours, e_hf32)
+    assert _normrel(got, ref32) < 1e-3
+    assert torch.isfinite(got).all()
+
+
+@pytest.mark.parametrize("cfg", [MambaConfig(d_model=64, n_layer=2, vocab_size=100), mamba_130m()],
+                         ids=["small", "130m"])
+def test_prefill_then_decode_matches_forward(cuda_device, cfg):
+    """Prompt of 100 tokens, then 24 single-token steps through the scan's
+    h0/h_last: the logits equal those of one forward over all 124 tokens."""
+    model = MambaLM(cfg).init_random(seed=11).to(cuda_device)
+    ids = _ids(cfg.vocab_size, 124, 3, cuda_device, batch=2)
+    full = model(ids)
+    logits, state = model.prefill(ids[:, :100])
+    tol = 1e-5 if cfg.n_layer == 2 else 1e-3
+    assert _normrel(logits, full[:, :100]) < tol
+    steps = torch.stack([model.step(ids[:, t], state) for t in range(100, 124)], dim=1)
+    assert _normrel(steps, full[:, 100:]) < tol
+
+
+def test_cuda_graph_replay_equals_eager(cuda_device):
+    model = MambaLM(mamba_130m()).init_random(seed=0).to(cuda_device)
+    ids, logits, graph = model.capture(1, 256)
+    x = _ids(model.cfg.vocab_size, 256, 5, cuda_device)
+    ids.copy_(x)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(logits, model(x))
