@@ -149,6 +149,31 @@ __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __
 __device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
 __device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
 
+// 2^x for a pair, on the FMA pipe instead of the SFU: x = j + f with j =
+// round(x) (adding 1.5*2^23 rounds to an integer in the low mantissa bits)
+// and f in [-1/2, 1/2]; 2^f by a degree-6 polynomial (relative-error
+// near-minimax fit on [-1/2, 1/2], coefficients fitted for this code; max
+// relative error 7.9e-8 in float32 Horner form, under one ulp); then j is
+// added to the exponent field. x is clamped to [-125, 127] so the result is
+// always a normal float: 2^x below 2^-125 comes out as ~2^-125 instead of
+// 0 (an absolute difference under 3e-38), above 2^127 as 2^127.
+__device__ __forceinline__ float2 exp2_fma2(float2 x) {
+  x = make_float2(fminf(fmaxf(x.x, -125.f), 127.f), fminf(fmaxf(x.y, -125.f), 127.f));
+  const float2 t = add2(x, make_float2(12582912.f, 12582912.f));
+  const float2 j = add2(t, make_float2(-12582912.f, -12582912.f));
+  const float2 f = fma2(j, make_float2(-1.f, -1.f), x);  // x - j, exact
+  float2 p = make_float2(1.534580806037411e-4f, 1.534580806037411e-4f);
+  p = fma2(p, f, make_float2(1.3399930903688073e-3f, 1.3399930903688073e-3f));
+  p = fma2(p, f, make_float2(9.618489071726799e-3f, 9.618489071726799e-3f));
+  p = fma2(p, f, make_float2(5.550328642129898e-2f, 5.550328642129898e-2f));
+  p = fma2(p, f, make_float2(0.24022646248340607f, 0.24022646248340607f));
+  p = fma2(p, f, make_float2(0.6931471824645996f, 0.6931471824645996f));
+  p = fma2(p, f, make_float2(1.f, 1.f));
+  // bits(t) = bits(1.5*2^23) + j, and bits(1.5*2^23) << 23 wraps to 0
+  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
+}
+
 __device__ __forceinline__ float lg2_approx(float x) {
   float y;
   asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

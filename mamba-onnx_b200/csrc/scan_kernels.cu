@@ -44,8 +44,24 @@ constexpr int kAcc = MAMBA_SCAN_ACC;
 
 // --------------------------------------------------------------- tile math
 
+#ifndef MAMBA_SCAN_POLY_EMIT
+#define MAMBA_SCAN_POLY_EMIT 0
+#endif
+#ifndef MAMBA_SCAN_POLY_AGG
+#define MAMBA_SCAN_POLY_AGG 1
+#endif
+// Exact variants: of the 8 state pairs of a step, this many take abar =
+// 2^(delta*A*log2 e) from exp2_fma2 (FMA pipe), the rest from the SFU. The
+// aggregate pass has FMA capacity to spare (no C.h contraction) and its 16
+// SFU exponentials per step bound it, so one pair moves there (Exact
+// 1x2048x16384: 312 -> 295 us); the emit pass is not SFU-bound and keeps all
+// of them on the SFU.
+template <int M> struct PolyPairs {
+  static constexpr int value = (M == kEmit) ? MAMBA_SCAN_POLY_EMIT : MAMBA_SCAN_POLY_AGG;
+};
+
 // abar and B*delta*u of one step, for the lane's 16 states.
-template <int V>
+template <int V, int M>
 __device__ __forceinline__ void step_prep(const float* __restrict__ Bt_, float dt, float du,
                                           const float2 (&Ar)[8], float2 (&a)[8], float2 (&bu)[8]) {
   using Tr = VariantTraits<V>;
@@ -60,8 +76,11 @@ __device__ __forceinline__ void step_prep(const float* __restrict__ Bt_, float d
       // abar = exp(delta*A) = 2^(delta * A*log2(e)); Ar holds A*log2(e)
       const float2 x0 = mul2(dt2, Ar[2 * q]);
       const float2 x1 = mul2(dt2, Ar[2 * q + 1]);
-      a[2 * q] = make_float2(ex2_approx(x0.x), ex2_approx(x0.y));
-      a[2 * q + 1] = make_float2(ex2_approx(x1.x), ex2_approx(x1.y));
+      a[2 * q] = (2 * q < PolyPairs<M>::value) ? exp2_fma2(x0)
+                                               : make_float2(ex2_approx(x0.x), ex2_approx(x0.y));
+      a[2 * q + 1] = (2 * q + 1 < PolyPairs<M>::value)
+                         ? exp2_fma2(x1)
+                         : make_float2(ex2_approx(x1.x), ex2_approx(x1.y));
     } else {
       // abar = 1 + delta*A (cc:275-282 written as (1+dA)h + dBu)
       a[2 * q] = fma2(dt2, Ar[2 * q], one2);
@@ -146,7 +165,7 @@ __device__ __forceinline__ void compute_tile(const float* us,
 #pragma unroll
   for (int k = 0; k < 8; ++k) du[k] = mul2(dt[k], uu[k]);
   float2 a[8], bu[8];
-  step_prep<V>(Bs, dt[0].x, du[0].x, Ar, a, bu);
+  step_prep<V, M>(Bs, dt[0].x, du[0].x, Ar, a, bu);
   float2 s_prev = make_float2(0.f, 0.f);
   float2 yy[8];
 #pragma unroll
@@ -163,7 +182,7 @@ __device__ __forceinline__ void compute_tile(const float* us,
     }
     if (t + 1 < kT) {
       const int k = (t + 1) >> 1;
-      step_prep<V>(Bs + (t + 1) * kN, ((t + 1) & 1) ? dt[k].y : dt[k].x,
+      step_prep<V, M>(Bs + (t + 1) * kN, ((t + 1) & 1) ? dt[k].y : dt[k].x,
                    ((t + 1) & 1) ? du[k].y : du[k].x, Ar, a, bu);
     }
     if (M == kEmit) {
