@@ -24,7 +24,7 @@
 extern "C" {
 #endif
 
-#define MAMBA_SCAN_ABI_VERSION 1
+#define MAMBA_SCAN_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define MAMBA_SCAN_API __attribute__((visibility("default")))
@@ -134,6 +134,18 @@ MAMBA_SCAN_API const char* mamba_scan_status_string(int status);
  * (MAMBA_SCAN_OK or MAMBA_SCAN_ERR_DEVICE_TIMEOUT). Diagnostic only.
  */
 MAMBA_SCAN_API int mamba_scan_check_device_error(void);
+
+/*
+ * Self-test of the device-side failure detection (no counterpart in the
+ * reference, which has no device code). Enqueues on `stream` one CTA whose
+ * mbarrier wait can never complete (a transaction is announced that no copy
+ * delivers) and which gives up after limit_ns nanoseconds (0 < limit_ns <=
+ * 10 s), exactly as a scan kernel's tile wait gives up after 2 s. A following
+ * mamba_scan_check_device_error() returns MAMBA_SCAN_ERR_DEVICE_TIMEOUT; the
+ * context stays usable. Nothing faults and nothing is left in flight.
+ * Returns MAMBA_SCAN_OK once enqueued.
+ */
+MAMBA_SCAN_API int mamba_scan_selftest_wait_timeout(int64_t limit_ns, void* stream);
 
 /* MAMBA_SCAN_ABI_VERSION of the loaded library. */
 MAMBA_SCAN_API int mamba_scan_abi_version(void);

@@ -335,6 +335,16 @@ int mamba_scan_check_device_error(void) {
   return code;
 }
 
+int mamba_scan_selftest_wait_timeout(int64_t limit_ns, void* stream) {
+  t_last_error.clear();
+  if (limit_ns <= 0 || limit_ns > 10000000000LL)
+    return fail(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "limit_ns must be in (0, 10 s]");
+  const cudaError_t e =
+      mamba_scan::launch_wait_selftest((uint64_t)limit_ns, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
+  return MAMBA_SCAN_OK;
+}
+
 int mamba_scan_abi_version(void) { return MAMBA_SCAN_ABI_VERSION; }
 
 }  // extern "C"

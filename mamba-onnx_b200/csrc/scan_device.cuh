@@ -16,6 +16,7 @@ constexpr int kRows = 32;  // (b, d) rows per CTA: one warp, one row per lane
 constexpr int kT = 16;     // time steps per tile: 64-byte rows in shared memory
 constexpr int kStages = 3;  // tiles in the shared-memory ring
 constexpr int kCarryThreads = 256;  // threads per CTA of the carry kernel
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // a tile wait gives up after 2 s
 
 enum Variant { kLinear = 0, kExact = 1, kFused = 2, kFusedExact = 3 };
 enum Mode { kEmit = 0, kAggregate = 1 };
@@ -72,19 +73,21 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
-// Bounded wait on an mbarrier phase. Gives up after ~2 s of wall time, records
-// MAMBA_SCAN_ERR_DEVICE_TIMEOUT (6) in *err and returns false, so a lost
-// transaction can never hang the GPU.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+// Bounded wait on an mbarrier phase. Gives up after limit_ns of wall time
+// (2 s for the scan kernels), records MAMBA_SCAN_ERR_DEVICE_TIMEOUT (6) in
+// *err and returns false, so a lost transaction can never hang the GPU.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = globaltimer_ns();
-  for (uint32_t spins = 0;; ++spins) {
+  // the iteration cap backs up the clock check (each try_wait already
+  // suspends for a while before it fails)
+  for (uint32_t spins = 0; spins < (1u << 26); ++spins) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((spins & 255u) == 255u && globaltimer_ns() - start > 2000000000ull) {
-      atomicExch(err, 6);
-      return false;
-    }
+    if ((spins & 255u) == 255u && globaltimer_ns() - start > limit_ns) break;
   }
+  atomicExch(err, 6);  // MAMBA_SCAN_ERR_DEVICE_TIMEOUT
+  return false;
 }
 
 // 3-D tiled TMA load into shared memory, completing on `bar`.

@@ -493,6 +493,30 @@ __global__ void __launch_bounds__(kCarryThreads) carry_kernel(const ScanParams p
   }
 }
 
+// ------------------------------------------------------- wait self-test
+
+// Exercises the bounded wait's give-up path without any fault: one arrival
+// announces 16 bytes of transaction that no copy will ever deliver, so the
+// phase cannot complete; mbar_wait gives up after limit_ns and records
+// MAMBA_SCAN_ERR_DEVICE_TIMEOUT. No asynchronous copy is issued, so nothing
+// is in flight when the CTA exits.
+__global__ void __launch_bounds__(32) wait_selftest_kernel(uint64_t limit_ns) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbarrier_init();
+  }
+  __syncwarp();
+  if (threadIdx.x == 0) mbar_arrive_expect_tx(&bar, 16);
+  __syncwarp();
+  mbar_wait(&bar, 0, &g_scan_device_error, limit_ns);
+}
+
+cudaError_t launch_wait_selftest(uint64_t limit_ns, cudaStream_t stream) {
+  wait_selftest_kernel<<<1, 32, 0, stream>>>(limit_ns);
+  return cudaGetLastError();
+}
+
 // ------------------------------------------------------------------ launch
 
 // Launch `kernel` on `st`; with `pdl` as a programmatic dependent launch (the

@@ -61,6 +61,10 @@ cudaError_t launch_scan_kernel(int variant, int mode, bool tma, const ScanParams
 // plan), as a programmatic dependent launch.
 cudaError_t launch_carry_kernel(const ScanParams& p, cudaStream_t stream);
 
+// One CTA whose mbarrier wait cannot complete and gives up after limit_ns
+// (see mamba_scan_selftest_wait_timeout).
+cudaError_t launch_wait_selftest(uint64_t limit_ns, cudaStream_t stream);
+
 // Resident CTAs per SM of one kernel instantiation (occupancy calculator).
 cudaError_t max_blocks_per_sm(int variant, int mode, bool tma, int* blocks);
 

@@ -72,6 +72,8 @@ def library() -> ctypes.CDLL:
         lib.mamba_scan_launch_static_workspace.restype = ctypes.c_int
         lib.mamba_scan_launch_static_workspace.argtypes = [ctypes.c_int, ctypes.POINTER(ScanArgs),
                                                            ctypes.c_void_p]
+        lib.mamba_scan_selftest_wait_timeout.restype = ctypes.c_int
+        lib.mamba_scan_selftest_wait_timeout.argtypes = [ctypes.c_int64, ctypes.c_void_p]
         _lib = lib
     return _lib
 
@@ -173,3 +175,12 @@ def launch_static_workspace(op_id: int, args: ScanArgs, stream_handle) -> int:
 def check_device_error() -> int:
     """Synchronise and return/clear the kernels' device error word (0 = none)."""
     return int(library().mamba_scan_check_device_error())
+
+
+def selftest_wait_timeout(limit_ns: int, stream=None) -> int:
+    """Enqueue the bounded-wait self-test (a wait that must give up after
+    limit_ns); check_device_error() then returns MAMBA_SCAN_ERR_DEVICE_TIMEOUT."""
+    import torch
+
+    st = stream if stream is not None else torch.cuda.current_stream()
+    return int(library().mamba_scan_selftest_wait_timeout(int(limit_ns), st.cuda_stream))

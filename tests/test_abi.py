@@ -46,7 +46,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_abi_version_and_status_strings():
     lib = cuda.library()
-    assert lib.mamba_scan_abi_version() == 1
+    assert lib.mamba_scan_abi_version() == 2
     assert lib.mamba_scan_status_string(2) == b"unsupported dstate"
     assert lib.mamba_scan_status_string(99) == b"unknown status"
 

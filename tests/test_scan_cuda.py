@@ -235,3 +235,23 @@ def test_linearity_in_u_at_full_length(op):
 
 def test_no_device_error_recorded():
     assert cuda.check_device_error() == 0
+
+
+def test_bounded_wait_gives_up_and_the_context_survives():
+    """A wait that cannot complete (announced bytes that no copy delivers)
+    gives up after its limit and records MAMBA_SCAN_ERR_DEVICE_TIMEOUT; the
+    next scan runs normally. No fault is involved."""
+    import time
+
+    assert cuda.check_device_error() == 0
+    t0 = time.perf_counter()
+    assert cuda.selftest_wait_timeout(20_000_000) == 0  # 20 ms
+    assert cuda.check_device_error() == 6
+    assert time.perf_counter() - t0 < 5.0
+    assert cuda.check_device_error() == 0  # read clears it
+    assert cuda.selftest_wait_timeout(0) == 1  # limit out of range: nothing launched
+    u, delta, A, B, C, D, z = [None if a is None else dev(a) for a in
+                               sc.config_inputs(1, 64, 256, True, seed=4)[:7]]
+    out = cuda.selective_scan("SelectiveScanFused", u, delta, A, B, C, D, z)
+    assert torch.isfinite(out).all()
+    assert cuda.check_device_error() == 0
