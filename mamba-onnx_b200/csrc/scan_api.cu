@@ -23,7 +23,7 @@ using mamba_scan::TmaMaps;
 
 constexpr int kRows = 32;
 constexpr int kTile = 16;
-constexpr int64_t kMinChunk = 32;
+constexpr int64_t kMinChunk = 32;  // chunks are multiples of 32 steps (two tiles), at least one
 
 thread_local std::string t_last_error;
 
@@ -75,7 +75,7 @@ Plan make_plan(int64_t batch, int64_t dim, int64_t seqlen, int sms, int slots) {
   const int64_t wave = std::max<int64_t>(1, (int64_t)slots * sms);
   pl.n_full = N;
   pl.chunk_len = seqlen;
-  if (N <= 0 || seqlen <= 2 * kMinChunk) return pl;
+  if (N <= 0 || seqlen <= kMinChunk) return pl;
   int64_t tail = 0, want = 0;
   if (N < subparts) {
     tail = N;
@@ -89,7 +89,7 @@ Plan make_plan(int64_t batch, int64_t dim, int64_t seqlen, int sms, int slots) {
     if (want < 3) return pl;
   }
   int64_t len = round_up((seqlen + want - 1) / want, kMinChunk);
-  len = std::max<int64_t>(len, 2 * kMinChunk);
+  len = std::max<int64_t>(len, kMinChunk);
   const int64_t n = (seqlen + len - 1) / len;
   if (n < 2 || n > 4096) return pl;
   pl.n_full = N - tail;
