@@ -27,6 +27,12 @@ replay of the forward; value in tokens/s (all ranks; each rank runs its own
 replica, no collective). Its cpu_baseline (and --impl reference) is the same
 forward on the host: torch CPU GEMMs with the reference's C++ plugin doing
 the scans.
+
+    python bench.py --workload mamba130m-decode [--gpus N] [--steps K]
+
+Single-token decode of the same model after a 1024-token prefill: one step =
+one CUDA-graph replay of the decode step (scans through h0/h_last), value in
+tokens/s. The reference has no decode path (--impl reference says so).
 """
 from __future__ import annotations
 
@@ -235,11 +241,14 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ncu-case", action="store_true",
                     help="for profilers: build the inputs, run warmup+steps calls, print nothing timed")
-    ap.add_argument("--workload", choices=["scan", "mamba130m"], default="scan")
+    ap.add_argument("--workload", choices=["scan", "mamba130m", "mamba130m-decode"],
+                    default="scan")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.workload == "mamba130m":
         return run_model(args)
+    if args.workload == "mamba130m-decode":
+        return run_decode(args)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -615,6 +624,101 @@ def run_model(args):
         print(json.dumps(line), flush=True)
     if world > 1:
         del graph, sgraph
+        dist.destroy_process_group()
+
+
+DECODE_BATCH, DECODE_PROMPT = 1, 1024
+DECODE_WORKLOAD = ("Mamba-130m single-token decode (24 blocks, fp32), batch 1 per GPU after a "
+                   "1024-token prefill; each step one CUDA-graph replay of the step (every scan "
+                   "is SelectiveScanFusedExact with seqlen 1 through h0/h_last)")
+
+
+def run_decode(args):
+    """Decode tokens/s: one step = one token for each sequence of the batch."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable":
+                              "the reference has no decode path (its op always starts from a zero "
+                              "state); see --workload mamba130m for the reference forward"}))
+        return
+    import torch
+    import torch.distributed as dist
+
+    from mamba_onnx.model import MambaLM, mamba_130m
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    B = DECODE_BATCH
+    model = MambaLM(mamba_130m()).init_random(0).to(device)
+    g = torch.Generator(device=device).manual_seed(SEED + rank)
+    prompt = torch.randint(0, model.cfg.vocab_size, (B, DECODE_PROMPT), device=device, generator=g)
+    _, state = model.prefill(prompt)
+    ids, logits, g_state, graph = model.capture_step(B)
+    model.copy_state(g_state, state)
+    ids.copy_(prompt[:, -1])
+    stream = torch.cuda.current_stream(device)
+
+    def timed(fn, n):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(n):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / n
+
+    def max_over_ranks(ms):
+        if world == 1:
+            return ms
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    with ClockSampler(device) as clocks:
+        ms = max_over_ranks(timed(graph.replay, args.steps))
+
+    # end to end: next token ids from pinned host memory, greedy token back
+    host_ids = ids.cpu().pin_memory()
+    host_next = torch.empty(B, dtype=torch.int64).pin_memory()
+
+    def e2e_step():
+        ids.copy_(host_ids, non_blocking=True)
+        graph.replay()
+        host_next.copy_(torch.argmax(logits, dim=-1), non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(timed(e2e_step, max(3, args.e2e_steps * 10)))
+    if rank == 0:
+        print(json.dumps({
+            "metric": "Mamba-130m decode tokens/s", "value": world * B / (ms * 1e-3),
+            "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic (random init with Mamba's initialisation)",
+            "config": {"workload": DECODE_WORKLOAD, "batch_per_gpu": B, "global_batch": B * world,
+                       "prompt": DECODE_PROMPT,
+                       "parallelism": f"replica per GPU x{world}, no collective"},
+            "e2e": {"value": world * B / (e2e_ms * 1e-3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": host_ids.numel() * 8,
+                    "d2h_bytes_per_step": host_next.numel() * 8, "ms_per_step": e2e_ms,
+                    "path": "pinned token ids -> graph replay -> argmax token to host"},
+            "gpu_launches": model.cfg.n_layer * args.steps,
+            "clocks": clocks.summary()}), flush=True)
+    if world > 1:
+        del graph
         dist.destroy_process_group()
 
 

@@ -227,6 +227,34 @@ class MambaLM(torch.nn.Module):
         return self._head(h)[:, 0]
 
     @torch.no_grad()
+    def capture_step(self, batch: int, warmup: int = 3):
+        """CUDA-graph one decoding step. Returns (ids, logits, state, graph):
+        load a DecodeState into ``state`` (``copy_state``; e.g. from
+        ``prefill``), write the next token ids into ``ids``, ``graph.replay()``,
+        read ``logits``; ``state`` advances by one token per replay."""
+        dev = self.embedding.device
+        ids = torch.zeros(batch, dtype=torch.int64, device=dev)
+        state = self.new_state(batch)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                self.step(ids, state)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            logits = self.step(ids, state)
+        for t in state.conv + state.ssm:
+            t.zero_()
+        return ids, logits, state, graph
+
+    @staticmethod
+    @torch.no_grad()
+    def copy_state(dst: DecodeState, src: DecodeState):
+        for a, b in zip(dst.conv + dst.ssm, src.conv + src.ssm):
+            a.copy_(b)
+
+    @torch.no_grad()
     def capture(self, batch: int, seqlen: int, warmup: int = 3):
         """CUDA-graph the forward for a fixed shape. Returns (ids, logits, graph):
         write token ids into ``ids``, ``graph.replay()``, read ``logits``."""

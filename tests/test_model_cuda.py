@@ -99,3 +99,19 @@ def test_cuda_graph_replay_equals_eager(cuda_device):
     graph.replay()
     torch.cuda.synchronize()
     assert torch.equal(logits, model(x))
+
+
+def test_captured_decode_step_equals_eager(cuda_device):
+    """Prefill a prompt, then decode 8 tokens with the CUDA-graphed step and
+    with the eager step from the same state: identical logits."""
+    model = MambaLM(mamba_130m()).init_random(seed=1).to(cuda_device)
+    ids = _ids(model.cfg.vocab_size, 72, 6, cuda_device, batch=2)
+    _, state = model.prefill(ids[:, :64])
+    g_ids, g_logits, g_state, graph = model.capture_step(2)
+    model.copy_state(g_state, state)
+    for t in range(64, 72):
+        g_ids.copy_(ids[:, t])
+        graph.replay()
+        eager = model.step(ids[:, t], state)
+        torch.cuda.synchronize()
+        assert torch.equal(g_logits, eager), t
