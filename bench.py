@@ -28,6 +28,12 @@ replica, no collective). Its cpu_baseline (and --impl reference) is the same
 forward on the host: torch CPU GEMMs with the reference's C++ plugin doing
 the scans.
 
+    python bench.py --workload scan-b64 [--gpus N] [--steps K]
+
+SelectiveScanFused on a fixed total batch of 64 x 5120 x 4096 sharded by batch
+over the N GPUs (strong scaling); value from the compute time alone, the NCCL
+gather of the output to rank 0 timed separately (gather_ms).
+
     python bench.py --workload mamba130m-decode [--gpus N] [--steps K]
 
 Single-token decode of the same model after a 1024-token prefill: one step =
@@ -241,7 +247,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ncu-case", action="store_true",
                     help="for profilers: build the inputs, run warmup+steps calls, print nothing timed")
-    ap.add_argument("--workload", choices=["scan", "mamba130m", "mamba130m-decode"],
+    ap.add_argument("--workload", choices=["scan", "scan-b64", "mamba130m", "mamba130m-decode"],
                     default="scan")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
@@ -249,6 +255,8 @@ def main():
         return run_model(args)
     if args.workload == "mamba130m-decode":
         return run_decode(args)
+    if args.workload == "scan-b64":
+        return run_scan_b64(args)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -624,6 +632,131 @@ def run_model(args):
         print(json.dumps(line), flush=True)
     if world > 1:
         del graph, sgraph
+        dist.destroy_process_group()
+
+
+B64_BATCH, B64_SEQLEN, B64_SEED = 64, 4096, 3
+B64_WORKLOAD = (f"SelectiveScanFused fp32, total batch {B64_BATCH} x d_inner {DIM} x seqlen "
+                f"{B64_SEQLEN}, d_state {NSTATE}, sharded by batch across the GPUs; the output "
+                f"gathered to rank 0 by NCCL (timed separately)")
+
+
+def run_scan_b64(args):
+    """Strong scaling of the scan over a fixed batch of 64 (one shard per rank)."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        if rank == 0:
+            from oracle import oracle
+
+            cpu = reference_sample(oracle.host_threads(), 3)
+            print(json.dumps({"impl": "reference", "metric": METRIC, "value": cpu["value"],
+                              "unit": UNIT, "n_gpus": args.gpus, "cpu_baseline": cpu,
+                              "config": {"workload": B64_WORKLOAD,
+                                         "step": "one reference plugin call on 1x5120x2048"},
+                              "e2e": {"value": cpu["value"], "unit": UNIT,
+                                      "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+        return
+    import torch
+    import torch.distributed as dist
+
+    from mamba_onnx import cuda
+    from mamba_onnx.distributed import gather_output, shard_plan
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+    plan = shard_plan(B64_BATCH, DIM, world, rank)
+    if plan.axis != 0 or len(set(plan.sizes)) != 1:
+        raise SystemExit("scan-b64 needs a GPU count that divides 64")
+    nb, D, L = plan.length, DIM, B64_SEQLEN
+    # every batch entry from its own seed, so a rank's shard equals the slice
+    # of the single-GPU tensors
+    u = torch.empty(nb, D, L, device=device)
+    z, delta = torch.empty_like(u), torch.empty_like(u)
+    Bm = torch.empty(nb, L, NSTATE, device=device)
+    Cm = torch.empty_like(Bm)
+    g = torch.Generator(device=device)
+    g.manual_seed(B64_SEED)
+    lo, hi = float(np.log(1e-3)), float(np.log(1e-1))
+    dt = torch.exp(torch.rand(D, device=device, generator=g) * (hi - lo) + lo)
+    bias = torch.log(torch.expm1(dt))[:, None]
+    for i in range(nb):
+        g.manual_seed(B64_SEED * 1000003 + plan.start + i)
+        for t in (u[i], z[i], delta[i], Bm[i], Cm[i]):
+            t.normal_(generator=g)
+        delta[i].mul_(0.5).add_(bias)
+    A = -torch.arange(1, NSTATE + 1, device=device, dtype=torch.float32).repeat(D, 1)
+    Dv = torch.ones(D, device=device)
+    out = torch.empty_like(u)
+    ws = torch.empty(max(1, cuda.workspace_size(OP, nb, D, L)), dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def step():
+        cuda.selective_scan(OP, u, delta, A, Bm, Cm, Dv, z, out=out, workspace=ws, stream=stream)
+
+    def timed(fn, n):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(n):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / n
+
+    def max_over_ranks(ms):
+        if world == 1:
+            return ms
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    with ClockSampler(device) as clocks:
+        ms = max_over_ranks(timed(step, args.steps))
+    gather_ms = None
+    if world > 1:
+        full = torch.empty(B64_BATCH, D, L, device=device) if rank == 0 else None
+        gather_output(out, plan, out=full)  # warm-up
+        torch.cuda.synchronize()
+        dist.barrier()
+        gather_ms = max_over_ranks(timed(lambda: gather_output(out, plan, out=full), 5))
+        del full
+    if rank == 0:
+        hbm_peak, peak_kind = measured_peaks()
+        algo = algorithmic_bytes(nb, D, L)
+        achieved = algo / (ms * 1e-3) / 1e9
+        total = B64_BATCH * D * L * NSTATE
+        line = {
+            "metric": METRIC, "value": total / (ms * 1e-3), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": B64_WORKLOAD, "op": OP, "global_batch": B64_BATCH,
+                       "batch_per_gpu": nb, "d_inner": D, "seqlen": L, "d_state": NSTATE,
+                       "parallelism": f"batch-sharded x{world}; NCCL gather of out to rank 0",
+                       "l2": f"inputs {algo / 1e9:.2f} GB per GPU, larger than L2; no flush"},
+            "gather_ms": gather_ms,
+            "gather_bytes_to_rank0": (B64_BATCH - nb) * D * L * 4 if world > 1 else 0,
+            "compute_plus_gather_ms": ms + (gather_ms or 0.0),
+            "e2e": {"value": None, "note": "host-buffer end to end is measured on the default "
+                                           "workload (this one holds up to 21.5 GB per GPU)"},
+            "gpu_launches": (3 if ws.numel() > 1 else 1) * args.steps,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": achieved / hbm_peak, "per": "rank's op call",
+                         "peak_source": f"{peak_kind} hbm_gbs"},
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
         dist.destroy_process_group()
 
 

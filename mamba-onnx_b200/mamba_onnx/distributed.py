@@ -70,17 +70,25 @@ def scan_shard(op: str, plan: ShardPlan, u, delta, A, B, C, D, z=None, delta_bia
     return cuda.selective_scan(op, u, delta, A, B, C, D, z, delta_bias=delta_bias, **kw)
 
 
-def gather_output(out_local, plan: ShardPlan, group=None, dst: int = 0):
+def gather_output(out_local, plan: ShardPlan, group=None, dst: int = 0, out=None):
     """Collect every rank's output shard on rank `dst`; returns the full tensor there.
 
-    Shards are padded to the largest shard along the split axis so one gather
-    carries uneven splits; other ranks return None.
+    With a batch split of equal shards and `out` (the full [batch, dim, seqlen]
+    tensor, on `dst` only) the shards land directly in their slices of `out`.
+    Otherwise shards are padded to the largest shard along the split axis so
+    one gather carries uneven splits, and the result is concatenated. Other
+    ranks return None.
     """
     import torch
     import torch.distributed as dist
 
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
+    if plan.axis == 0 and len(set(plan.sizes)) == 1 and (out is not None or rank != dst):
+        n = plan.sizes[0]
+        bufs = [out.narrow(0, r * n, n) for r in range(world)] if rank == dst else None
+        dist.gather(out_local.contiguous(), bufs, dst=dst, group=group)
+        return out if rank == dst else None
     biggest = max(plan.sizes)
     if plan.length < biggest:
         pad_shape = list(out_local.shape)
@@ -92,4 +100,6 @@ def gather_output(out_local, plan: ShardPlan, group=None, dst: int = 0):
     if rank != dst:
         return None
     parts = [b.narrow(plan.axis, 0, n) for b, n in zip(bufs, plan.sizes)]
+    if out is not None:
+        return torch.cat(parts, dim=plan.axis, out=out)
     return torch.cat(parts, dim=plan.axis)

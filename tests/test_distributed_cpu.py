@@ -38,7 +38,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, batch, dim, op, q):
+def _worker(rank, world, port, batch, dim, op, q, into_out=False):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
@@ -53,7 +53,10 @@ def _worker(rank, world, port, batch, dim, op, q):
                                                           t(D), t(z))
         n = lambda x: None if x is None else x.numpy()  # noqa: E731
         local = oracle.scan_f64(op, n(lu), n(ld), n(lA), n(lB), n(lC), n(lD), n(lz))
-        full = gather_output(torch.from_numpy(local), plan)
+        out = torch.empty(batch, dim, 24, dtype=torch.float64) if into_out and rank == 0 else None
+        full = gather_output(torch.from_numpy(local), plan, out=out)
+        if out is not None:
+            assert full is out
         if rank == 0:
             ref = oracle.scan_f64(op, u, delta, A, B, C, D, z)
             q.put(("ok", float(np.abs(full.numpy() - ref).max()), tuple(full.shape)))
@@ -64,16 +67,18 @@ def _worker(rank, world, port, batch, dim, op, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,batch,dim,op", [
-    (2, 4, 40, "SelectiveScanFused"),      # batch split
-    (2, 1, 37, "SelectiveScanExact"),      # d_inner split (batch < world), uneven
-    (3, 5, 16, "SelectiveScan"),           # uneven batch split
+@pytest.mark.parametrize("world,batch,dim,op,into_out", [
+    (2, 4, 40, "SelectiveScanFused", False),   # batch split
+    (2, 4, 40, "SelectiveScanFused", True),    # even batch split, straight into `out`
+    (2, 1, 37, "SelectiveScanExact", False),   # d_inner split (batch < world), uneven
+    (3, 5, 16, "SelectiveScan", False),        # uneven batch split
+    (3, 5, 16, "SelectiveScan", True),         # uneven: padded gather, concatenated into `out`
 ])
-def test_sharded_scan_gathers_to_rank0(world, batch, dim, op):
+def test_sharded_scan_gathers_to_rank0(world, batch, dim, op, into_out):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, batch, dim, op, q))
+    procs = [ctx.Process(target=_worker, args=(r, world, port, batch, dim, op, q, into_out))
              for r in range(world)]
     for p in procs:
         p.start()
