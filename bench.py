@@ -247,6 +247,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ncu-case", action="store_true",
                     help="for profilers: build the inputs, run warmup+steps calls, print nothing timed")
+    ap.add_argument("--case", default=None, metavar="OP:B:D:L",
+                    help="with --ncu-case: another op and shape (benchmark-configuration "
+                         "distributions; non-fused ops draw delta per element)")
     ap.add_argument("--workload", choices=["scan", "scan-b64", "mamba130m", "mamba130m-decode"],
                     default="scan")
     args = ap.parse_args()
@@ -257,6 +260,8 @@ def main():
         return run_decode(args)
     if args.workload == "scan-b64":
         return run_scan_b64(args)
+    if args.ncu_case and args.case:
+        return run_case(args)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -633,6 +638,39 @@ def run_model(args):
     if world > 1:
         del graph, sgraph
         dist.destroy_process_group()
+
+
+def run_case(args):
+    """Profiling helper: warmup + steps calls of one op on one shape, nothing timed."""
+    import torch
+
+    from mamba_onnx import cuda
+
+    op, B, D, L = args.case.split(":")
+    B, D, L = int(B), int(D), int(L)
+    fused = "Fused" in op
+    device = torch.device("cuda", 0)
+    g = torch.Generator(device=device).manual_seed(SEED)
+    kw = dict(device=device, generator=g)
+    u = torch.randn(B, D, L, **kw)
+    z = torch.randn(B, D, L, **kw) if fused else None
+    Bm, Cm = torch.randn(B, L, NSTATE, **kw), torch.randn(B, L, NSTATE, **kw)
+    lo, hi = float(np.log(1e-3)), float(np.log(1e-1))
+    if fused:
+        dt = torch.exp(torch.rand(D, **kw) * (hi - lo) + lo)
+        delta = torch.randn(B, D, L, **kw) * 0.5 + torch.log(torch.expm1(dt))[None, :, None]
+    else:
+        delta = torch.exp(torch.rand(B, D, L, **kw) * (hi - lo) + lo)
+    A = -torch.arange(1, NSTATE + 1, device=device, dtype=torch.float32).repeat(D, 1)
+    Dv = torch.ones(D, device=device)
+    out = torch.empty_like(u)
+    ws_bytes = cuda.workspace_size(op, B, D, L)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=device)
+    for _ in range(args.warmup + args.steps):
+        cuda.selective_scan(op, u, delta, A, Bm, Cm, Dv, z, out=out, workspace=ws)
+    torch.cuda.synchronize()
+    print(json.dumps({"ncu_case": args.case, "launches_per_call": 3 if ws_bytes else 1,
+                      "calls": args.warmup + args.steps}))
 
 
 B64_BATCH, B64_SEQLEN, B64_SEED = 64, 4096, 3

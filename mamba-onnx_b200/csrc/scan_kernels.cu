@@ -457,6 +457,7 @@ __global__ void __launch_bounds__(kRows, MAMBA_SCAN_MIN_BLOCKS)
 // chunk c reads it. Launched after the aggregate pass as a programmatic
 // dependent launch: it lets the emit pass be scheduled at once, then waits
 // for the aggregate pass.
+template <int kAhead>  // chunks whose loads are in flight together
 __global__ void __launch_bounds__(kCarryThreads) carry_kernel(const ScanParams p) {
   pdl_trigger();
   const int64_t gid = (int64_t)blockIdx.x * kCarryThreads + threadIdx.x;
@@ -471,7 +472,6 @@ __global__ void __launch_bounds__(kCarryThreads) carry_kernel(const ScanParams p
   pdl_wait();
   const int n = p.n_chunks - 1;
   float* w = p.ws + ws_row * (int64_t)n * 2 * kN + s;
-  constexpr int kAhead = 8;  // chunks whose loads are in flight together
   for (int c = 0; c < n; c += kAhead) {
     float he[kAhead], pe[kAhead];
 #pragma unroll
@@ -563,7 +563,11 @@ cudaError_t launch_scan_kernel(int variant, int mode, bool tma, const ScanParams
 cudaError_t launch_carry_kernel(const ScanParams& p, cudaStream_t stream) {
   const int64_t threads = (int64_t)p.n_tail * kRows * kN;
   const unsigned blocks = (unsigned)((threads + kCarryThreads - 1) / kCarryThreads);
-  return launch(carry_kernel, blocks, kCarryThreads, stream, true, p);
+  // Up to 8 chunk aggregates per row: a small kernel (its CTAs wait resident
+  // beside the emit pass's whole row tiles, so they must stay light); more:
+  // 32 in flight, one load round trip for up to 33 chunks.
+  if (p.n_chunks - 1 <= 8) return launch(carry_kernel<8>, blocks, kCarryThreads, stream, true, p);
+  return launch(carry_kernel<32>, blocks, kCarryThreads, stream, true, p);
 }
 
 template <int V>
