@@ -37,9 +37,12 @@ namespace mamba_scan {
 __device__ int g_scan_device_error = 0;
 
 #ifndef MAMBA_SCAN_ACC
-#define MAMBA_SCAN_ACC 2
+#define MAMBA_SCAN_ACC 1
 #endif
-// Independent partial sums per step in the C.h contraction (2, 4 or 8).
+// Independent partial sums per step in the C.h contraction (1, 2, 4 or 8).
+// One chain measured best: the contraction of step t overlaps the state
+// update of step t+1, and the single chain saves the FADD2 that joins two
+// partial sums (SelectiveScanFused 1x1536x1024: 26.0 -> 25.2 us).
 constexpr int kAcc = MAMBA_SCAN_ACC;
 
 // --------------------------------------------------------------- tile math
@@ -60,14 +63,47 @@ template <int M> struct PolyPairs {
   static constexpr int value = (M == kEmit) ? MAMBA_SCAN_POLY_EMIT : MAMBA_SCAN_POLY_AGG;
 };
 
-// abar and B*delta*u of one step, for the lane's 16 states.
+#ifndef MAMBA_SCAN_WSCALE
+#define MAMBA_SCAN_WSCALE 1
+#endif
+
+// Linear variants (SelectiveScan, SelectiveScanFused) run the recurrence on
+// a rescaled state. With w_t = delta_t * u_t,
+//
+//   h_t = (1 + delta_t A) h_{t-1} + w_t B_t
+//
+// becomes, for g_t = h_t / w_t and r_t = w_{t-1} / w_t,
+//
+//   g_t = r_t (1 + delta_t A) g_{t-1} + B_t,   y_t = w_t (C_t . g_t) + D u_t,
+//
+// so B enters unscaled and the per-state multiply delta*u*B disappears: the
+// state update costs abar' = fma(r*delta, A, r) and one FMA, three FP32
+// operations per (row, step, state) with the contraction instead of four.
+// w is kept away from zero: |w| < kWMin takes kWMin (the input term then
+// differs from w*B by at most 2*kWMin*|B|). At the start of a pass w_{-1} = 1
+// (g = h), and the state leaves as h = w_last * g. The exact variants keep
+// abar = exp(delta*A) and the product delta*u*B (a positive w is not
+// guaranteed, so r cannot be folded into the exponent).
+constexpr float kWMin = 1e-12f;
+
+__device__ __forceinline__ float safe_w(float w) { return fabsf(w) < kWMin ? kWMin : w; }
+
+template <int V> struct Scaled {
+  static constexpr bool value = MAMBA_SCAN_WSCALE && !VariantTraits<V>::exact;
+};
+
+// abar and the input term of one step, for the lane's 16 states.
+// Exact variants: (x0, x1) = (delta, delta*u); a = exp(delta*A), bu = delta*u*B.
+// Linear variants: (x0, x1) = (r*delta, r) on the rescaled state,
+// a = r*(1 + delta*A), bu = B (unscaled: MAMBA_SCAN_WSCALE=0 keeps
+// (x0, x1) = (delta, delta*u), a = 1 + delta*A, bu = delta*u*B).
 template <int V, int M>
-__device__ __forceinline__ void step_prep(const float* __restrict__ Bt_, float dt, float du,
+__device__ __forceinline__ void step_prep(const float* __restrict__ Bt_, float x0_, float x1_,
                                           const float2 (&Ar)[8], float2 (&a)[8], float2 (&bu)[8]) {
   using Tr = VariantTraits<V>;
   const float2 one2 = make_float2(1.f, 1.f);
-  const float2 dt2 = make_float2(dt, dt);
-  const float2 du2 = make_float2(du, du);
+  const float2 dt2 = make_float2(x0_, x0_);
+  const float2 du2 = make_float2(x1_, x1_);
   const float4* Bt = reinterpret_cast<const float4*>(Bt_);
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
@@ -81,13 +117,22 @@ __device__ __forceinline__ void step_prep(const float* __restrict__ Bt_, float d
       a[2 * q + 1] = (2 * q + 1 < PolyPairs<M>::value)
                          ? exp2_fma2(x1)
                          : make_float2(ex2_approx(x1.x), ex2_approx(x1.y));
+    } else if (Scaled<V>::value) {
+      // abar' = r*(1 + delta*A) = fma(r*delta, A, r)
+      a[2 * q] = fma2(dt2, Ar[2 * q], du2);
+      a[2 * q + 1] = fma2(dt2, Ar[2 * q + 1], du2);
     } else {
       // abar = 1 + delta*A (cc:275-282 written as (1+dA)h + dBu)
       a[2 * q] = fma2(dt2, Ar[2 * q], one2);
       a[2 * q + 1] = fma2(dt2, Ar[2 * q + 1], one2);
     }
-    bu[2 * q] = mul2(du2, make_float2(bq.x, bq.y));
-    bu[2 * q + 1] = mul2(du2, make_float2(bq.z, bq.w));
+    if (Scaled<V>::value) {
+      bu[2 * q] = make_float2(bq.x, bq.y);
+      bu[2 * q + 1] = make_float2(bq.z, bq.w);
+    } else {
+      bu[2 * q] = mul2(du2, make_float2(bq.x, bq.y));
+      bu[2 * q + 1] = mul2(du2, make_float2(bq.z, bq.w));
+    }
   }
 }
 
@@ -131,7 +176,7 @@ __device__ __forceinline__ void compute_tile(const float* us,
                                              const float* __restrict__ Cs, float* os,
                                              int row, float2 (&h)[8], float2 (&P)[8], float& S,
                                              const float2 (&Ar)[8], float dskip, float bias,
-                                             float bias_l2e, int n_valid) {
+                                             float bias_l2e, int n_valid, float& w_prev) {
   using Tr = VariantTraits<V>;
   const float2 bias_l2e2 = make_float2(bias_l2e, bias_l2e);
   const float2 dskip2 = make_float2(dskip, dskip);
@@ -164,6 +209,20 @@ __device__ __forceinline__ void compute_tile(const float* us,
   }
 #pragma unroll
   for (int k = 0; k < 8; ++k) du[k] = mul2(dt[k], uu[k]);
+  // Linear variants on the rescaled state: from here dt holds r*delta, du
+  // holds r, and ww holds w = delta*u (kept away from zero).
+  float2 ww[8], dsk[8];
+  if (Scaled<V>::value) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      ww[k] = make_float2(safe_w(du[k].x), safe_w(du[k].y));
+      const float2 inv = make_float2(rcp_approx(ww[k].x), rcp_approx(ww[k].y));
+      du[k] = make_float2(w_prev * inv.x, ww[k].x * inv.y);  // r = w_{t-1} / w_t
+      w_prev = ww[k].y;
+      dt[k] = mul2(du[k], dt[k]);
+      if (M == kEmit) dsk[k] = mul2(dskip2, uu[k]);
+    }
+  }
   float2 a[8], bu[8];
   step_prep<V, M>(Bs, dt[0].x, du[0].x, Ar, a, bu);
   float2 s_prev = make_float2(0.f, 0.f);
@@ -189,7 +248,10 @@ __device__ __forceinline__ void compute_tile(const float* us,
       const float2 s = contract(Cs + t * kN, h);
       if (t & 1) {
         float2 y = make_float2(s_prev.x + s_prev.y, s.x + s.y);
-        y = fma2(dskip2, uu[t >> 1], y);                      // + D*u (cc:297)
+        if (Scaled<V>::value)
+          y = fma2(ww[t >> 1], y, dsk[t >> 1]);               // w*(C.g) + D*u (cc:297)
+        else
+          y = fma2(dskip2, uu[t >> 1], y);                    // + D*u (cc:297)
         yy[t >> 1] = Tr::fused ? mul2(y, gate[t >> 1]) : y;   // * silu(z) (cc:300-302)
       } else {
         s_prev = s;
@@ -314,6 +376,7 @@ __global__ void __launch_bounds__(kRows, MAMBA_SCAN_MIN_BLOCKS)
   // carry-in state of the chunks before them.
   float2 h[8], P[8];
   float S = 0.f;
+  float w_prev = 1.f;  // linear variants: the state runs as g = h / w (w_{-1} = 1)
 #pragma unroll
   for (int n = 0; n < 8; ++n) {
     h[n] = make_float2(0.f, 0.f);
@@ -382,10 +445,10 @@ __global__ void __launch_bounds__(kRows, MAMBA_SCAN_MIN_BLOCKS)
       float* os = sm.u[s];  // outputs overwrite this tile's u
       if (n_valid == kT)
         compute_tile<V, M, false>(sm.u[s], sm.dl[s], sm.z[s], sm.B[s], sm.C[s], os, lane, h, P, S,
-                                  Ar, dskip, bias, bias_l2e, n_valid);
+                                  Ar, dskip, bias, bias_l2e, n_valid, w_prev);
       else
         compute_tile<V, M, true>(sm.u[s], sm.dl[s], sm.z[s], sm.B[s], sm.C[s], os, lane, h, P, S,
-                                 Ar, dskip, bias, bias_l2e, n_valid);
+                                 Ar, dskip, bias, bias_l2e, n_valid, w_prev);
       if (M == kEmit) {
         fence_proxy_async_smem();
         __syncwarp();
@@ -413,10 +476,10 @@ __global__ void __launch_bounds__(kRows, MAMBA_SCAN_MIN_BLOCKS)
       float* os = sm.u[0];
       if (n_valid == kT)
         compute_tile<V, M, false>(sm.u[0], sm.dl[0], sm.z[0], sm.B[0], sm.C[0], os, lane,
-                                  h, P, S, Ar, dskip, bias, bias_l2e, n_valid);
+                                  h, P, S, Ar, dskip, bias, bias_l2e, n_valid, w_prev);
       else
         compute_tile<V, M, true>(sm.u[0], sm.dl[0], sm.z[0], sm.B[0], sm.C[0], os, lane,
-                                 h, P, S, Ar, dskip, bias, bias_l2e, n_valid);
+                                 h, P, S, Ar, dskip, bias, bias_l2e, n_valid, w_prev);
       __syncwarp();
       if (M == kEmit) store_tile_plain(os, p, b, d0, t0, lane);
       __syncwarp();
@@ -424,6 +487,13 @@ __global__ void __launch_bounds__(kRows, MAMBA_SCAN_MIN_BLOCKS)
   }
 
   if (!row_ok) return;
+  if (Scaled<V>::value) {  // back to h (and, for the aggregates, to prod(abar))
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      h[n] = mul2(h[n], make_float2(w_prev, w_prev));
+      P[n] = mul2(P[n], make_float2(w_prev, w_prev));
+    }
+  }
   if (M == kEmit) {
     if (p.h_last != nullptr && chunk == n_chunks - 1) {
 #pragma unroll
