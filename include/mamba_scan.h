@@ -92,8 +92,9 @@ MAMBA_SCAN_API size_t mamba_scan_workspace_size(int variant, int64_t batch, int6
 /*
  * Enqueue one selective scan on `stream` (a cudaStream_t; NULL = the legacy
  * default stream). `workspace` may be NULL (workspace_bytes ignored); when it
- * is not NULL it must hold at least mamba_scan_workspace_size(...) bytes and be
- * 16-byte aligned. Returns a mamba_scan_status; on failure nothing was
+ * is not NULL it must hold at least mamba_scan_workspace_size(...) bytes, be
+ * 16-byte aligned, and its workspace_bytes must not overlap out, h_last or
+ * any input (MAMBA_SCAN_ERR_ALIASING). Returns a mamba_scan_status; on failure nothing was
  * enqueued and mamba_scan_last_error() describes the cause.
  */
 MAMBA_SCAN_API int mamba_scan_launch(int variant, const mamba_scan_args* args, void* workspace,

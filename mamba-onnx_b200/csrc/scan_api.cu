@@ -236,6 +236,17 @@ int mamba_scan_launch(int variant, const mamba_scan_args* a, void* workspace,
   }
   if (overlaps(a->out, big, a->h_last, state_bytes))
     return fail(MAMBA_SCAN_ERR_ALIASING, "h_last overlaps out");
+  // The caller's whole workspace region must be disjoint from every tensor:
+  // the aggregate pass writes it while the emit pass reads the inputs.
+  if (workspace != nullptr && workspace_bytes > 0) {
+    if (overlaps(workspace, workspace_bytes, a->out, big))
+      return fail(MAMBA_SCAN_ERR_ALIASING, "workspace overlaps out");
+    if (overlaps(workspace, workspace_bytes, a->h_last, state_bytes))
+      return fail(MAMBA_SCAN_ERR_ALIASING, "workspace overlaps h_last");
+    for (int i = 0; i < 8; ++i)
+      if (overlaps(workspace, workspace_bytes, ins[i], in_bytes[i]))
+        return fail(MAMBA_SCAN_ERR_ALIASING, "workspace overlaps an input");
+  }
 
   ScanParams p{};
   p.u = a->u;
@@ -286,8 +297,6 @@ int mamba_scan_launch(int variant, const mamba_scan_args* a, void* workspace,
                                                 std::to_string(need));
     } else if (!aligned16(workspace)) {
       return fail(MAMBA_SCAN_ERR_WORKSPACE, "workspace must be 16-byte aligned");
-    } else if (overlaps(workspace, need, a->out, big)) {
-      return fail(MAMBA_SCAN_ERR_ALIASING, "workspace overlaps out");
     }
   }
 

@@ -83,6 +83,17 @@ def test_launch_rejects_aliasing_output():
     assert lib.mamba_scan_launch(0, ctypes.byref(a), None, 0, None) == 4
 
 
+@pytest.mark.parametrize("field", ["u", "delta", "z", "B", "C", "A", "D", "out"])
+def test_launch_rejects_workspace_overlapping_a_tensor(field):
+    """The workspace is written while the inputs are read: no overlap allowed."""
+    lib = cuda.library()
+    a = _args()
+    ws = getattr(a, field) + 8
+    rc = lib.mamba_scan_launch(2, ctypes.byref(a), ws, 64, None)
+    assert rc == 4
+    assert "workspace overlaps" in lib.mamba_scan_last_error().decode()
+
+
 def test_empty_batch_is_a_no_op():
     lib = cuda.library()
     assert lib.mamba_scan_launch(0, ctypes.byref(_args(batch=0)), None, 0, None) == 0
