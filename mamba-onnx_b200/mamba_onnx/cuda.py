@@ -74,6 +74,12 @@ def library() -> ctypes.CDLL:
                                                            ctypes.c_void_p]
         lib.mamba_scan_selftest_wait_timeout.restype = ctypes.c_int
         lib.mamba_scan_selftest_wait_timeout.argtypes = [ctypes.c_int64, ctypes.c_void_p]
+        lib.mamba_rmsnorm.restype = ctypes.c_int
+        lib.mamba_rmsnorm.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int64] * 2 + \
+            [ctypes.c_float, ctypes.c_void_p]
+        lib.mamba_causal_conv1d_silu.restype = ctypes.c_int
+        lib.mamba_causal_conv1d_silu.argtypes = [ctypes.c_void_p, ctypes.c_int64] + \
+            [ctypes.c_void_p] * 3 + [ctypes.c_int64] * 4 + [ctypes.c_void_p]
         _lib = lib
     return _lib
 
@@ -184,3 +190,60 @@ def selftest_wait_timeout(limit_ns: int, stream=None) -> int:
 
     st = stream if stream is not None else torch.cuda.current_stream()
     return int(library().mamba_scan_selftest_wait_timeout(int(limit_ns), st.cuda_stream))
+
+
+# ---- kernels of the Mamba block around the scan (include/mamba_model_ops.h) ----
+
+def _raise(rc, what):
+    lib = library()
+    raise ScanError(rc, f"{what}: {lib.mamba_scan_status_string(rc).decode()}: "
+                        f"{lib.mamba_scan_last_error().decode()}")
+
+
+def rmsnorm(x, weight, eps: float, out=None, stream=None):
+    """RMSNorm over the last dimension of a contiguous CUDA float32 tensor:
+    x * rsqrt(mean(x^2, -1) + eps) * weight. Returns ``out`` (new if None)."""
+    import torch
+
+    cols = x.shape[-1]
+    _check("x", x, tuple(x.shape))
+    _check("weight", weight, (cols,))
+    if out is None:
+        out = torch.empty_like(x)
+    else:
+        _check("out", out, tuple(x.shape))
+    st = stream if stream is not None else torch.cuda.current_stream(x.device)
+    rc = library().mamba_rmsnorm(_ptr(x), _ptr(weight), _ptr(out), x.numel() // cols, cols,
+                                 float(eps), st.cuda_stream)
+    if rc != STATUS_OK:
+        _raise(rc, "rmsnorm")
+    return out
+
+
+def causal_conv1d_silu(x, weight, bias=None, out=None, stream=None):
+    """silu(causal depthwise conv1d over the sequence): x [B, D, L] CUDA float32
+    whose rows are contiguous and D-stride is L (e.g. the first half of the
+    in_proj output [B, 2D, L]); weight [D, 1, K] or [D, K]; bias [D] or None.
+    Equals F.silu(F.conv1d(x, weight, bias, padding=K-1, groups=D)[..., :L]).
+    Returns ``out`` ([B, D, L], new if None)."""
+    import torch
+
+    if x.dim() != 3 or not x.is_cuda or x.dtype != torch.float32:
+        raise TypeError("x must be a [batch, dim, seqlen] CUDA float32 tensor")
+    batch, dim, seqlen = x.shape
+    if (seqlen > 1 and x.stride(2) != 1) or (dim > 1 and x.stride(1) != seqlen):
+        raise ValueError("x rows must be contiguous with dim stride seqlen")
+    w = weight.reshape(dim, -1)
+    _check("weight", w, (dim, w.shape[1]))
+    _check("bias", bias, (dim,))
+    if out is None:
+        out = torch.empty((batch, dim, seqlen), dtype=torch.float32, device=x.device)
+    else:
+        _check("out", out, (batch, dim, seqlen))
+    st = stream if stream is not None else torch.cuda.current_stream(x.device)
+    bstride = x.stride(0) if batch > 1 else dim * seqlen
+    rc = library().mamba_causal_conv1d_silu(_ptr(x), bstride, _ptr(w), _ptr(bias), _ptr(out),
+                                            batch, dim, seqlen, w.shape[1], st.cuda_stream)
+    if rc != STATUS_OK:
+        _raise(rc, "causal_conv1d_silu")
+    return out

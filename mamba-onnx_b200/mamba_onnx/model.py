@@ -14,7 +14,9 @@ is the numerical reference.
 Everything is float32. ``forward`` runs a whole sequence; ``step`` decodes one
 token from a ``DecodeState`` (the convolution window and the 16 scan states
 per channel), which the scan carries in through ``h0`` and out through
-``h_last``.
+``h_last``. On CUDA tensors the RMSNorms and the causal convolution + SiLU run
+on this package's kernels too (include/mamba_model_ops.h); on CPU tensors the
+same arithmetic runs as torch operations.
 """
 from __future__ import annotations
 
@@ -49,6 +51,31 @@ class MambaConfig:
         return self.dt_rank or math.ceil(self.d_model / 16)
 
 
+def rms_norm(x, weight, eps: float):
+    """x * rsqrt(mean(x^2, -1) + eps) * weight (one CUDA kernel on CUDA tensors)."""
+    if x.is_cuda:
+        return cuda.rmsnorm(x.contiguous(), weight, eps)
+    var = x.pow(2).mean(-1, keepdim=True)
+    return x * torch.rsqrt(var + eps) * weight
+
+
+def conv_silu(x, weight, bias):
+    """silu(causal depthwise conv1d over the last axis): x [B, D, L] (rows
+    contiguous, e.g. the first half of the in_proj output), weight [D, 1, K]."""
+    if x.is_cuda:
+        return cuda.causal_conv1d_silu(x, weight, bias)
+    K, L = weight.shape[-1], x.shape[-1]
+    return F.silu(F.conv1d(x, weight, bias, padding=K - 1, groups=x.shape[1])[..., :L])
+
+
+def add_out_proj(h, y, weight):
+    """h + y^T W^T for h [B, L, d], y [B, D, L]; with one batch entry the sum is
+    the GEMM's own accumulation (addmm), not a separate kernel."""
+    if h.shape[0] == 1:
+        return torch.addmm(h[0], y[0].t(), weight.t()).unsqueeze(0)
+    return h + torch.matmul(y.transpose(1, 2), weight.t())
+
+
 def mamba_130m() -> MambaConfig:
     """Mamba-130m: 24 blocks, d_model 768, d_inner 1536, d_state 16, dt_rank 48."""
     return MambaConfig()
@@ -74,17 +101,27 @@ class MambaLayer(torch.nn.Module):
         self.out_proj_weight = torch.nn.Parameter(torch.empty(d, D, **f32))
 
     def _norm(self, x):
-        var = x.pow(2).mean(-1, keepdim=True)
-        return x * torch.rsqrt(var + self.cfg.rms_eps) * self.norm_weight
+        return rms_norm(x, self.norm_weight, self.cfg.rms_eps)
 
     def _ssm_inputs(self, x):
         """x [B, D, L] after conv + SiLU -> delta [B, D, L] (before bias), B, C [B, L, N]."""
         N, R = self.cfg.d_state, self.cfg.rank
-        x_dbl = torch.matmul(x.transpose(1, 2), self.x_proj_weight.t())  # [B, L, R + 2N]
-        delta = torch.matmul(self.dt_proj_weight, x_dbl[..., :R].transpose(1, 2))  # [B, D, L]
+        if x.shape[0] == 1:  # 2-D GEMMs take the transposed views without copies
+            x_dbl = torch.mm(x[0].t(), self.x_proj_weight.t()).unsqueeze(0)  # [1, L, R + 2N]
+            delta = torch.mm(self.dt_proj_weight, x_dbl[0, :, :R].t()).unsqueeze(0)
+        else:
+            x_dbl = torch.matmul(x.transpose(1, 2), self.x_proj_weight.t())  # [B, L, R + 2N]
+            delta = torch.matmul(self.dt_proj_weight, x_dbl[..., :R].transpose(1, 2))  # [B, D, L]
         Bm = x_dbl[..., R:R + N].contiguous()
         Cm = x_dbl[..., R + N:].contiguous()
         return delta, Bm, Cm
+
+    def _in_proj(self, h):
+        """rmsnorm(h) [B, L, d] -> in_proj output xz [B, 2D, L] (x rows, then z rows)."""
+        hn = self._norm(h)
+        if h.shape[0] == 1:
+            return torch.mm(self.in_proj_weight, hn[0].t()).unsqueeze(0)
+        return torch.matmul(self.in_proj_weight, hn.transpose(1, 2))
 
     def forward(self, h, A, conv_state=None, ssm_state=None, scan=None):
         """h [B, L, d_model] -> h + mixer(norm(h)); A = -exp(A_log). Given
@@ -93,22 +130,21 @@ class MambaLayer(torch.nn.Module):
         replaces the CUDA op (same signature as cuda.selective_scan)."""
         scan = scan or cuda.selective_scan
         D, L, K = self.cfg.d_inner, h.shape[1], self.cfg.d_conv
-        xz = torch.matmul(self.in_proj_weight, self._norm(h).transpose(1, 2))  # [B, 2D, L]
-        x = F.silu(F.conv1d(xz[:, :D], self.conv_weight, self.conv_bias,
-                            padding=K - 1, groups=D)[..., :L])
+        xz = self._in_proj(h)  # [B, 2D, L]
+        x = conv_silu(xz[:, :D], self.conv_weight, self.conv_bias)
         z = xz[:, D:].contiguous()
         delta, Bm, Cm = self._ssm_inputs(x)
         y = scan(SCAN_OP, x, delta, A, Bm, Cm, self.D, z, delta_bias=self.dt_proj_bias,
                  h_last=ssm_state)
         if conv_state is not None:  # the last K inputs of the convolution, zero-padded
             conv_state.copy_(F.pad(xz[:, :D], (max(0, K - L), 0))[..., -K:])
-        return h + torch.matmul(y.transpose(1, 2), self.out_proj_weight.t())
+        return add_out_proj(h, y, self.out_proj_weight)
 
     def step(self, h, A, conv_state, ssm_state):
         """One token: h [B, 1, d_model]; conv_state [B, D, d_conv] (last inputs of
         the convolution, oldest first) and ssm_state [B, D, N] are updated."""
         D = self.cfg.d_inner
-        xz = torch.matmul(self.in_proj_weight, self._norm(h).transpose(1, 2))  # [B, 2D, 1]
+        xz = self._in_proj(h)  # [B, 2D, 1]
         conv_state.copy_(torch.cat([conv_state[..., 1:], xz[:, :D]], dim=-1))
         x = torch.sum(conv_state * self.conv_weight[:, 0, :], dim=-1) + self.conv_bias
         x = F.silu(x).unsqueeze(-1).contiguous()  # [B, D, 1]
@@ -118,7 +154,7 @@ class MambaLayer(torch.nn.Module):
         y = cuda.selective_scan(SCAN_OP, x, delta, A, Bm, Cm, self.D, z,
                                 delta_bias=self.dt_proj_bias, h0=ssm_state, h_last=new_state)
         ssm_state.copy_(new_state)
-        return h + torch.matmul(y.transpose(1, 2), self.out_proj_weight.t())
+        return add_out_proj(h, y, self.out_proj_weight)
 
 
 @dataclass
@@ -189,8 +225,7 @@ class MambaLM(torch.nn.Module):
     # ---------------------------------------------------------------- forward
 
     def _head(self, h):
-        var = h.pow(2).mean(-1, keepdim=True)
-        h = h * torch.rsqrt(var + self.cfg.rms_eps) * self.norm_f_weight
+        h = rms_norm(h, self.norm_f_weight, self.cfg.rms_eps)
         return torch.matmul(h, self.embedding.t())
 
     @torch.no_grad()

@@ -94,6 +94,27 @@ def test_launch_rejects_workspace_overlapping_a_tensor(field):
     assert "workspace overlaps" in lib.mamba_scan_last_error().decode()
 
 
+def test_model_kernels_validate_before_launch():
+    """include/mamba_model_ops.h entry points reject bad arguments without CUDA."""
+    lib = cuda.library()
+    fake = 0x10000
+    # rmsnorm: cols must be positive; y must not overlap x
+    assert lib.mamba_rmsnorm(fake, fake * 2, fake * 3, 4, 0, 1e-5, None) == 1
+    assert lib.mamba_rmsnorm(fake, fake * 9, fake + 8, 4, 16, 1e-5, None) == 4
+    assert "overlaps" in lib.mamba_scan_last_error().decode()
+    assert lib.mamba_rmsnorm(fake, fake * 2, fake * 3, 0, 16, 1e-5, None) == 0  # no rows
+    # conv: width 1..8, batch stride >= dim * seqlen, y disjoint from x
+    assert lib.mamba_causal_conv1d_silu(fake, 64, fake * 2, None, fake * 3, 1, 4, 16, 9,
+                                        None) == 1
+    assert "width" in lib.mamba_scan_last_error().decode()
+    assert lib.mamba_causal_conv1d_silu(fake, 63, fake * 2, None, fake * 3, 2, 4, 16, 4,
+                                        None) == 1
+    assert lib.mamba_causal_conv1d_silu(fake, 64, fake * 2, None, fake + 16, 1, 4, 16, 4,
+                                        None) == 4
+    assert lib.mamba_causal_conv1d_silu(fake, 64, fake * 2, None, fake * 3, 1, 0, 16, 4,
+                                        None) == 0  # empty
+
+
 def test_empty_batch_is_a_no_op():
     lib = cuda.library()
     assert lib.mamba_scan_launch(0, ctypes.byref(_args(batch=0)), None, 0, None) == 0
