@@ -156,17 +156,94 @@ __device__ __forceinline__ float2 contract(const float* __restrict__ Ct_, const 
   return acc[0];
 }
 
-// One 16-step tile for the calling lane's row. Reads the swizzled u/delta/z
+// Per-step scalar work of one 16-step tile for the calling lane's row, on
+// packed pairs of consecutive steps (entry k holds steps 2k and 2k+1):
+//   dt, du  (delta, delta*u); on the rescaled state of the linear variants
+//           (r*delta, r) with r_t = w_{t-1} / w_t;
+//   ww      w = delta*u kept away from zero (rescaled state);
+//   dsk     D*u (rescaled state, emit); uu: u; gate: silu(z) (fused, emit).
+// Softplus (fused variants) is applied to delta first; kPartial zeroes delta
+// of the steps >= n_valid (the ragged last tile).
+struct TileScalars {
+  float2 uu[8], dt[8], du[8], gate[8], ww[8], dsk[8];
+};
+
+template <int V, int M, bool kPartial>
+__device__ __forceinline__ void tile_scalars(const float* us, const float* __restrict__ ds,
+                                             const float* __restrict__ zs, int row, float dskip,
+                                             float bias, float bias_l2e, int n_valid,
+                                             float& w_prev, TileScalars& ts) {
+  using Tr = VariantTraits<V>;
+  const float2 bias_l2e2 = make_float2(bias_l2e, bias_l2e);
+  const float2 dskip2 = make_float2(dskip, dskip);
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const int off = row * kT + (((c ^ (row >> 1)) & 3) << 2);
+    const float4 u4 = *reinterpret_cast<const float4*>(us + off);
+    const float4 d4 = *reinterpret_cast<const float4*>(ds + off);
+    ts.uu[2 * c] = make_float2(u4.x, u4.y);
+    ts.uu[2 * c + 1] = make_float2(u4.z, u4.w);
+    ts.dt[2 * c] = make_float2(d4.x, d4.y);
+    ts.dt[2 * c + 1] = make_float2(d4.z, d4.w);
+    if (Tr::fused) {
+      ts.dt[2 * c] = softplus2<Tr::exact>(ts.dt[2 * c], bias, bias_l2e2);
+      ts.dt[2 * c + 1] = softplus2<Tr::exact>(ts.dt[2 * c + 1], bias, bias_l2e2);
+      if (M == kEmit) {
+        const float4 z4 = *reinterpret_cast<const float4*>(zs + off);
+        ts.gate[2 * c] = silu2<Tr::exact>(make_float2(z4.x, z4.y));
+        ts.gate[2 * c + 1] = silu2<Tr::exact>(make_float2(z4.z, z4.w));
+      }
+    }
+  }
+  if (kPartial) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if (2 * k >= n_valid) ts.dt[k].x = 0.f;
+      if (2 * k + 1 >= n_valid) ts.dt[k].y = 0.f;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 8; ++k) ts.du[k] = mul2(ts.dt[k], ts.uu[k]);
+  // Linear variants on the rescaled state: from here dt holds r*delta, du
+  // holds r, and ww holds w = delta*u (kept away from zero).
+  if (Scaled<V>::value) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      ts.ww[k] = make_float2(safe_w(ts.du[k].x), safe_w(ts.du[k].y));
+      const float2 inv = make_float2(rcp_approx(ts.ww[k].x), rcp_approx(ts.ww[k].y));
+      ts.du[k] = make_float2(w_prev * inv.x, ts.ww[k].x * inv.y);  // r = w_{t-1} / w_t
+      w_prev = ts.ww[k].y;
+      ts.dt[k] = mul2(ts.du[k], ts.dt[k]);
+      if (M == kEmit) ts.dsk[k] = mul2(dskip2, ts.uu[k]);
+    }
+  }
+}
+
+// y of steps (2k, 2k+1) from their contractions (s0, s1) = (C.h of step 2k,
+// C.h of step 2k+1): + D*u (cc:297), * silu(z) (cc:300-302); on the rescaled
+// state y = w*(C.g) + D*u.
+template <int V>
+__device__ __forceinline__ float2 step_pair_output(const TileScalars& ts, int k, float s0, float s1,
+                                                   float dskip) {
+  using Tr = VariantTraits<V>;
+  float2 y = make_float2(s0, s1);
+  if (Scaled<V>::value)
+    y = fma2(ts.ww[k], y, ts.dsk[k]);
+  else
+    y = fma2(make_float2(dskip, dskip), ts.uu[k], y);
+  return Tr::fused ? mul2(y, ts.gate[k]) : y;
+}
+
+// One 16-step tile for the calling lane's row (row-per-lane layout: the lane
+// keeps all 16 states of its row in h[0..7]). Reads the swizzled u/delta/z
 // tiles and the B/C tiles, updates h (and the decay product P, or the delta
 // sum S, in aggregate mode) and, in emit mode, writes y into the swizzled
 // output tile `os` (which may be the u tile itself: every u value is read
-// before the first output is written). kPartial masks steps >= n_valid (the
-// ragged last tile).
+// before the first output is written).
 //
-// The per-step scalar work (softplus, delta*u, the silu gate, D*u) is done
-// first for all 16 steps, on packed pairs of consecutive steps. The state
-// loop then computes abar and B*delta*u of step t+1 before the C.h
-// contraction of step t, so the contraction overlaps the next step's
+// The per-step scalar work is done first for all 16 steps (tile_scalars).
+// The state loop then computes abar and the input term of step t+1 before
+// the C.h contraction of step t, so the contraction overlaps the next step's
 // independent work.
 template <int V, int M, bool kPartial>
 __device__ __forceinline__ void compute_tile(const float* us,
@@ -178,53 +255,10 @@ __device__ __forceinline__ void compute_tile(const float* us,
                                              const float2 (&Ar)[8], float dskip, float bias,
                                              float bias_l2e, int n_valid, float& w_prev) {
   using Tr = VariantTraits<V>;
-  const float2 bias_l2e2 = make_float2(bias_l2e, bias_l2e);
-  const float2 dskip2 = make_float2(dskip, dskip);
-  float2 uu[8], dt[8], du[8], gate[8];
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    const int off = row * kT + (((c ^ (row >> 1)) & 3) << 2);
-    const float4 u4 = *reinterpret_cast<const float4*>(us + off);
-    const float4 d4 = *reinterpret_cast<const float4*>(ds + off);
-    uu[2 * c] = make_float2(u4.x, u4.y);
-    uu[2 * c + 1] = make_float2(u4.z, u4.w);
-    dt[2 * c] = make_float2(d4.x, d4.y);
-    dt[2 * c + 1] = make_float2(d4.z, d4.w);
-    if (Tr::fused) {
-      dt[2 * c] = softplus2<Tr::exact>(dt[2 * c], bias, bias_l2e2);
-      dt[2 * c + 1] = softplus2<Tr::exact>(dt[2 * c + 1], bias, bias_l2e2);
-      if (M == kEmit) {
-        const float4 z4 = *reinterpret_cast<const float4*>(zs + off);
-        gate[2 * c] = silu2<Tr::exact>(make_float2(z4.x, z4.y));
-        gate[2 * c + 1] = silu2<Tr::exact>(make_float2(z4.z, z4.w));
-      }
-    }
-  }
-  if (kPartial) {
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      if (2 * k >= n_valid) dt[k].x = 0.f;
-      if (2 * k + 1 >= n_valid) dt[k].y = 0.f;
-    }
-  }
-#pragma unroll
-  for (int k = 0; k < 8; ++k) du[k] = mul2(dt[k], uu[k]);
-  // Linear variants on the rescaled state: from here dt holds r*delta, du
-  // holds r, and ww holds w = delta*u (kept away from zero).
-  float2 ww[8], dsk[8];
-  if (Scaled<V>::value) {
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      ww[k] = make_float2(safe_w(du[k].x), safe_w(du[k].y));
-      const float2 inv = make_float2(rcp_approx(ww[k].x), rcp_approx(ww[k].y));
-      du[k] = make_float2(w_prev * inv.x, ww[k].x * inv.y);  // r = w_{t-1} / w_t
-      w_prev = ww[k].y;
-      dt[k] = mul2(du[k], dt[k]);
-      if (M == kEmit) dsk[k] = mul2(dskip2, uu[k]);
-    }
-  }
+  TileScalars ts;
+  tile_scalars<V, M, kPartial>(us, ds, zs, row, dskip, bias, bias_l2e, n_valid, w_prev, ts);
   float2 a[8], bu[8];
-  step_prep<V, M>(Bs, dt[0].x, du[0].x, Ar, a, bu);
+  step_prep<V, M>(Bs, ts.dt[0].x, ts.du[0].x, Ar, a, bu);
   float2 s_prev = make_float2(0.f, 0.f);
   float2 yy[8];
 #pragma unroll
@@ -236,26 +270,20 @@ __device__ __forceinline__ void compute_tile(const float* us,
 #pragma unroll
         for (int n = 0; n < 8; ++n) P[n] = mul2(P[n], a[n]);
       } else {
-        S += (t & 1) ? dt[t >> 1].y : dt[t >> 1].x;
+        S += (t & 1) ? ts.dt[t >> 1].y : ts.dt[t >> 1].x;
       }
     }
     if (t + 1 < kT) {
       const int k = (t + 1) >> 1;
-      step_prep<V, M>(Bs + (t + 1) * kN, ((t + 1) & 1) ? dt[k].y : dt[k].x,
-                   ((t + 1) & 1) ? du[k].y : du[k].x, Ar, a, bu);
+      step_prep<V, M>(Bs + (t + 1) * kN, ((t + 1) & 1) ? ts.dt[k].y : ts.dt[k].x,
+                      ((t + 1) & 1) ? ts.du[k].y : ts.du[k].x, Ar, a, bu);
     }
     if (M == kEmit) {
       const float2 s = contract(Cs + t * kN, h);
-      if (t & 1) {
-        float2 y = make_float2(s_prev.x + s_prev.y, s.x + s.y);
-        if (Scaled<V>::value)
-          y = fma2(ww[t >> 1], y, dsk[t >> 1]);               // w*(C.g) + D*u (cc:297)
-        else
-          y = fma2(dskip2, uu[t >> 1], y);                    // + D*u (cc:297)
-        yy[t >> 1] = Tr::fused ? mul2(y, gate[t >> 1]) : y;   // * silu(z) (cc:300-302)
-      } else {
+      if (t & 1)
+        yy[t >> 1] = step_pair_output<V>(ts, t >> 1, s_prev.x + s_prev.y, s.x + s.y, dskip);
+      else
         s_prev = s;
-      }
     }
   }
   if (M == kEmit) {
