@@ -47,6 +47,34 @@ MAMBA_SCAN_API int mamba_causal_conv1d_silu(const float* x, int64_t x_batch_stri
                                             int64_t batch, int64_t dim, int64_t seqlen,
                                             int64_t width, void* stream);
 
+/*
+ * Split fp32 values into two tf32 parts for mamba_gemm_tf32x3:
+ *   hi = tf32(x), lo = tf32(x - hi)   (round to nearest; x - hi is exact),
+ * written as [rows][cols] with row stride `ld` (>= cols) into hi and lo.
+ * transpose = 0: x is [rows][cols] with row stride ldx (>= cols);
+ * transpose = 1: x is [cols][rows] with row stride ldx (>= rows), i.e. the
+ * output is the split transpose of x. Finite inputs only.
+ */
+MAMBA_SCAN_API int mamba_split_tf32(const float* x, int64_t rows, int64_t cols, int64_t ldx,
+                                    int transpose, float* hi, float* lo, int64_t ld,
+                                    void* stream);
+
+/*
+ * fp32-accurate GEMM on the tensor cores (3xTF32):
+ *   C[m][n] (+)= sum_k A[m][k] * B[n][k]   for m < M, n < N, k < K
+ * computed as A_hi B_hi + A_hi B_lo + A_lo B_hi with an fp32 accumulator,
+ * from the split operands of mamba_split_tf32: A parts [M][K] with row stride
+ * lda, B parts [N][K] with row stride ldb (lda, ldb >= K, multiples of 4; all
+ * four parts 16-byte aligned). C element (m, n) lives at c[m*ldc_m + n*ldc_n]
+ * (any strides; C must not overlap the operands). c_in = NULL writes the
+ * product; otherwise C = C_in + product, C_in laid out with C's strides (it
+ * may be C itself, or must not overlap C). K >= 1.
+ */
+MAMBA_SCAN_API int mamba_gemm_tf32x3(const float* a_hi, const float* a_lo, int64_t lda,
+                                     const float* b_hi, const float* b_lo, int64_t ldb,
+                                     const float* c_in, float* c, int64_t ldc_m, int64_t ldc_n,
+                                     int64_t M, int64_t N, int64_t K, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

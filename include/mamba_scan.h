@@ -131,8 +131,9 @@ MAMBA_SCAN_API const char* mamba_scan_status_string(int status);
 
 /*
  * Synchronises the current device, then returns and clears the device-side
- * error word that the kernels set when a bounded wait times out
- * (MAMBA_SCAN_OK or MAMBA_SCAN_ERR_DEVICE_TIMEOUT). Diagnostic only.
+ * error words that the kernels (the scan kernels and the model-ops GEMM of
+ * mamba_model_ops.h) set when a bounded wait times out (MAMBA_SCAN_OK or
+ * MAMBA_SCAN_ERR_DEVICE_TIMEOUT). Diagnostic only.
  */
 MAMBA_SCAN_API int mamba_scan_check_device_error(void);
 

@@ -1,0 +1,531 @@
+// fp32-accurate GEMM on the sm_100a tensor cores (3xTF32), for the dense
+// projections of a Mamba model around the scan op (in_proj, out_proj and
+// the tied LM head of a Mamba block stack; the reference project leaves
+// these GEMMs to its caller, benchmarks/profiler.py:18-150).
+//
+// C[m][n] (+)= sum_k A[m][k] * B[n][k], both operands K-contiguous, computed
+// as A_hi B_hi + A_hi B_lo + A_lo B_hi on tcgen05 TF32 MMAs with an FP32
+// accumulator in tensor memory, where X_hi = tf32(X) and X_lo = tf32(X -
+// X_hi) (round to nearest, mamba_split_tf32). Each product then carries a
+// relative error of at most ~3 * 2^-22 (the dropped X_lo Y_lo term and the
+// rounding of the lo parts), the same order as the fp32 rounding of the
+// accumulation itself.
+//
+// One CTA = one 128 x 128 output tile, 10 warps:
+// * warp 8 lane 0 (producer) streams 32-wide K blocks of A_hi, A_lo, B_hi,
+//   B_lo by TMA (128-byte swizzle, 4 x 16 KB per stage, 3-stage ring);
+// * warp 9 lane 0 (MMA issuer) waits for a stage, issues 4 K-steps x 3
+//   products of tcgen05.mma.kind::tf32 (M = 128, N = 128, K = 8) into a
+//   TMEM accumulator that starts from zero for every K block (corrections
+//   first, then hi*hi), and commits the stage back to the producer and the
+//   accumulator to the accumulator warps (two accumulators alternate);
+// * warps 0..7 (warp w owns TMEM lanes 32(w%4)..+31 = tile rows, and half
+//   of the columns) read each K block's sums (tcgen05.ld) and add them to
+//   fp32 registers, then store C with arbitrary strides, optionally adding
+//   a second matrix C_in (which may be C itself).
+// Every mbarrier wait is bounded (mamba_gemm error word on timeout).
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/mamba_model_ops.h"
+#include "../../include/mamba_scan.h"
+#include "scan_device.cuh"
+#include "scan_kernels.h"
+
+namespace mamba_gemm {
+
+using mamba_scan::smem_u32;
+
+constexpr int BM = 128, BN = 128, BK = 32;  // BK fp32 = 128 bytes: one swizzled row
+constexpr int kStages = 3;
+// warps 0..7 accumulate and store: warp w owns TMEM lanes 32(w%4)..+31
+// (tile rows) and columns [64(w/4), 64(w/4) + 64), so two warps share each
+// SM sub-partition and hide each other's TMEM load latency
+constexpr int kAccWarps = 8;
+constexpr int kAccThreads = 32 * kAccWarps;
+constexpr int kAccCols = BN * 4 / kAccWarps;  // 64
+constexpr int kProducerWarp = kAccWarps, kMmaWarp = kAccWarps + 1;
+constexpr int kThreads = 32 * (kAccWarps + 2);
+constexpr uint32_t kTileBytes = BM * BK * 4;  // 16 KB (BN == BM)
+constexpr uint32_t kStageBytes = 4 * kTileBytes;
+// Two fp32 accumulators of BN columns (alternate K blocks). The tensor
+// core's accumulation into TMEM loses accuracy with every update (on K =
+// 1536 one accumulator over the whole K ended 5x further from float64 than
+// an fp32 GEMM), so each K block starts from zero and the accumulator warps
+// fold it into fp32 registers with round-to-nearest adds. Within a block the
+// 8 correction products (~2^-11 of the sums) go first, while the
+// accumulator is small, then the 4 hi*hi products: the corrections' own
+// rounding stays at their scale.
+constexpr int kTmemCols = 2 * BN;
+
+struct __align__(1024) GemmSmem {
+  float a_hi[kStages][BM * BK];
+  float a_lo[kStages][BM * BK];
+  float b_hi[kStages][BN * BK];
+  float b_lo[kStages][BN * BK];
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint64_t acc_full[2];   // a K block's sums are in TMEM buffer b (tcgen05.commit)
+  uint64_t acc_empty[2];  // the accumulator warps have read buffer b
+  uint32_t tmem_base;
+};
+constexpr size_t kSmemBytes = sizeof(GemmSmem) + 1024;  // + room to align the base
+
+struct GemmMaps {
+  CUtensorMap a_hi, a_lo, b_hi, b_lo;
+};
+
+struct GemmParams {
+  float* c;
+  const float* c_in;  // NULL: C = A B^T; else C = C_in + A B^T (C's strides)
+  int64_t ldc_m, ldc_n;
+  int M, N, K;
+};
+
+__device__ int g_gemm_device_error = 0;
+
+// ------------------------------------------------------------ PTX wrappers
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major tile of rows of 32 fp32 (128
+// bytes) written by TMA with the 128-byte swizzle: start address >> 4 in
+// bits [0,14), leading byte offset 16 B (unused for swizzled K-major) in
+// [16,30), stride byte offset 1024 B (between 8-row groups) in [32,46),
+// descriptor version 1 in [46,48), base offset 0, layout type 2 =
+// SWIZZLE_128B in [61,64) (the sm_100 UMMA SmemDescriptor; CUTLASS
+// cute/arch/mma_sm100_desc.hpp).
+__device__ __forceinline__ uint64_t sw128_desc(const void* tile) {
+  const uint32_t a = smem_u32(tile);
+  return (uint64_t)((a >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor of kind::tf32, D = F32, A = B = TF32, both K-major,
+// N >> 3 in bits [17,23), M >> 4 in bits [24,29) (UMMA InstrDescriptor).
+constexpr uint32_t kInstrDesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                                ((uint32_t)(BM >> 4) << 24);
+
+__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t"
+      ".reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t"
+      "}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(kInstrDesc), "r"(accumulate)
+      : "memory");
+}
+
+// The mbarrier receives one arrival once every tcgen05 operation this
+// thread issued before has completed.
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+// 32 consecutive fp32 columns of this thread's TMEM lane (32x32b.x32);
+// complete only after tmem_wait().
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+      "%28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_wait() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// ------------------------------------------------------------------ kernel
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tf32x3_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  GemmSmem& sm = *reinterpret_cast<GemmSmem*>(
+      smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // M tiles vary fastest: the CTAs running together share B tiles (the
+  // larger operand of a wide GEMM such as an LM head), read from HBM once
+  const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
+  const int nk = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mamba_scan::mbar_init(&sm.full[s], 1);
+      mamba_scan::mbar_init(&sm.empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mamba_scan::mbar_init(&sm.acc_full[b], 1);
+      mamba_scan::mbar_init(&sm.acc_empty[b], kAccThreads);
+    }
+    mamba_scan::fence_mbarrier_init();
+  }
+  if (warp == kProducerWarp && lane == 0) {
+    mamba_scan::prefetch_tensormap(&maps.a_hi);
+    mamba_scan::prefetch_tensormap(&maps.a_lo);
+    mamba_scan::prefetch_tensormap(&maps.b_hi);
+    mamba_scan::prefetch_tensormap(&maps.b_lo);
+  }
+  if (warp == 0) {  // the whole warp allocates the accumulators' TMEM columns
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&sm.tmem_base)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  if (warp == kProducerWarp) {
+    if (lane == 0) {
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % kStages;
+        if (kb >= kStages &&
+            !mamba_scan::mbar_wait(&sm.empty[s], (uint32_t)((kb / kStages) - 1) & 1u,
+                                   &g_gemm_device_error))
+          break;
+        mamba_scan::mbar_arrive_expect_tx(&sm.full[s], kStageBytes);
+        const int k0 = kb * BK;
+        tma_load_2d(sm.a_hi[s], &maps.a_hi, &sm.full[s], k0, m0);
+        tma_load_2d(sm.a_lo[s], &maps.a_lo, &sm.full[s], k0, m0);
+        tma_load_2d(sm.b_hi[s], &maps.b_hi, &sm.full[s], k0, n0);
+        tma_load_2d(sm.b_lo[s], &maps.b_lo, &sm.full[s], k0, n0);
+      }
+    }
+    __syncwarp();
+  } else if (warp == kMmaWarp) {
+    if (lane == 0) {
+      // K block kb accumulates from zero into TMEM buffer kb & 1 (hi*hi in
+      // its first BN columns, the corrections in the next BN), which the
+      // accumulator warps drain before block kb + 2 reuses it.
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % kStages, b = kb & 1;
+        if (kb >= 2 && !mamba_scan::mbar_wait(&sm.acc_empty[b], (uint32_t)((kb >> 1) - 1) & 1u,
+                                              &g_gemm_device_error))
+          break;
+        if (!mamba_scan::mbar_wait(&sm.full[s], (uint32_t)(kb / kStages) & 1u,
+                                   &g_gemm_device_error))
+          break;
+        tc_fence_after();
+        const uint32_t t = tmem + (uint32_t)(b * BN);
+        const uint64_t ah = sw128_desc(sm.a_hi[s]), al = sw128_desc(sm.a_lo[s]);
+        const uint64_t bh = sw128_desc(sm.b_hi[s]), bl = sw128_desc(sm.b_lo[s]);
+#pragma unroll
+        for (int k = 0; k < BK / 8; ++k) {
+          const uint64_t off = (uint64_t)(k * 32) >> 4;  // 8 tf32 = 32 bytes along the row
+          mma_tf32(t, al + off, bh + off, k > 0 ? 1u : 0u);
+          mma_tf32(t, ah + off, bl + off, 1u);
+        }
+#pragma unroll
+        for (int k = 0; k < BK / 8; ++k) {
+          const uint64_t off = (uint64_t)(k * 32) >> 4;
+          mma_tf32(t, ah + off, bh + off, 1u);
+        }
+        mma_commit(&sm.empty[s]);     // the stage is free once these MMAs have read it
+        mma_commit(&sm.acc_full[b]);  // and the block's sums are ready
+      }
+    }
+    __syncwarp();
+  } else {
+    // accumulator warps: each thread keeps kAccCols sums of its tile row in
+    // registers, adding every K block's (hi*hi + corrections) with
+    // round-to-nearest fp32 adds (packed pairs).
+    const int quarter = warp & 3, col0 = (warp >> 2) * kAccCols;
+    float2 acc[kAccCols / 2];
+#pragma unroll
+    for (int j = 0; j < kAccCols / 2; ++j) acc[j] = make_float2(0.f, 0.f);
+    bool ok = true;
+    const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)col0;
+    for (int kb = 0; kb < nk; ++kb) {
+      const int b = kb & 1;
+      ok = mamba_scan::mbar_wait(&sm.acc_full[b], (uint32_t)(kb >> 1) & 1u, &g_gemm_device_error);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+      const uint32_t t = lane_base + (uint32_t)(b * BN);
+      uint32_t v[kAccCols];
+#pragma unroll
+      for (int c = 0; c < kAccCols; c += 32)
+        tmem_ld32(t + (uint32_t)c, *reinterpret_cast<uint32_t(*)[32]>(v + c));
+      tmem_wait();
+#pragma unroll
+      for (int j = 0; j < kAccCols / 2; ++j)
+        acc[j] = __fadd2_rn(acc[j], make_float2(__uint_as_float(v[2 * j]),
+                                                __uint_as_float(v[2 * j + 1])));
+      tc_fence_before();
+      mbar_arrive(&sm.acc_empty[b]);
+    }
+    const int64_t m = (int64_t)m0 + quarter * 32 + lane;
+    if (__all_sync(0xffffffffu, ok) && m < p.M) {
+#pragma unroll
+      for (int j = 0; j < kAccCols; ++j) {
+        const int64_t n = (int64_t)n0 + col0 + j;
+        const float a = (j & 1) ? acc[j / 2].y : acc[j / 2].x;
+        if (n < p.N) {
+          const int64_t o = m * p.ldc_m + n * p.ldc_n;
+          p.c[o] = p.c_in ? p.c_in[o] + a : a;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
+// --------------------------------------------------------- tf32 hi/lo split
+
+__device__ __forceinline__ float to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+// hi = tf32(x), lo = tf32(x - hi) (x - hi is exact in fp32).
+__device__ __forceinline__ void split1(float x, float& hi, float& lo) {
+  hi = to_tf32(x);
+  lo = to_tf32(x - hi);
+}
+
+// Row-contiguous source: grid (column blocks, rows); each thread splits 4
+// consecutive elements of one row (vector loads and stores when the row
+// starts and strides allow it).
+__global__ void split_rows_kernel(const float* __restrict__ x, int cols, int64_t ldx,
+                                  float* __restrict__ hi, float* __restrict__ lo, int64_t ld,
+                                  bool vec) {
+  const int64_t r = blockIdx.y;
+  const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  if (c >= cols) return;
+  const float* xr = x + r * ldx;
+  float* hr = hi + r * ld;
+  float* lr = lo + r * ld;
+  if (vec && c + 4 <= cols) {
+    const float4 v = __ldg(reinterpret_cast<const float4*>(xr + c));
+    float4 h, l;
+    split1(v.x, h.x, l.x);
+    split1(v.y, h.y, l.y);
+    split1(v.z, h.z, l.z);
+    split1(v.w, h.w, l.w);
+    *reinterpret_cast<float4*>(hr + c) = h;
+    *reinterpret_cast<float4*>(lr + c) = l;
+  } else {
+    for (int j = c; j < c + 4 && j < cols; ++j) split1(__ldg(xr + j), hr[j], lr[j]);
+  }
+}
+
+// Transposing source (out[r][c] = x[c][r], x rows of length ldx): 32 x 32
+// tiles through shared memory, coalesced on both sides.
+__global__ void split_transpose_kernel(const float* __restrict__ x, int rows, int cols,
+                                       int64_t ldx, float* __restrict__ hi,
+                                       float* __restrict__ lo, int64_t ld) {
+  __shared__ float t[32][33];
+  const int r0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
+  const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
+#pragma unroll
+  for (int j = ty; j < 32; j += 8) {
+    const int c = c0 + j, r = r0 + tx;  // x[c][r]
+    t[j][tx] = (c < cols && r < rows) ? __ldg(x + (int64_t)c * ldx + r) : 0.f;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int j = ty; j < 32; j += 8) {
+    const int r = r0 + j, c = c0 + tx;
+    if (r < rows && c < cols) {
+      float h, l;
+      split1(t[tx][j], h, l);
+      hi[(int64_t)r * ld + c] = h;
+      lo[(int64_t)r * ld + c] = l;
+    }
+  }
+}
+
+int read_and_clear_error() {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_gemm_device_error, sizeof(int)) != cudaSuccess) return -1;
+  if (v != 0) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_gemm_device_error, &zero, sizeof(int));
+  }
+  return v;
+}
+
+}  // namespace mamba_gemm
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 gemm_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// [rows][K] fp32, row stride ld floats, boxes of 32 K x 128 rows, 128-byte swizzle.
+bool encode_operand(PFN_cuTensorMapEncodeTiled_v12000 enc, CUtensorMap* m, const float* ptr,
+                    int64_t rows, int64_t K, int64_t ld) {
+  const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
+  const cuuint32_t box[2] = {mamba_gemm::BK, mamba_gemm::BM};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(ptr), dims, strides, box,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
+bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+bool overlap(const void* a, int64_t abytes, const void* b, int64_t bbytes) {
+  const auto a0 = reinterpret_cast<uintptr_t>(a), b0 = reinterpret_cast<uintptr_t>(b);
+  return a0 < b0 + (uintptr_t)bbytes && b0 < a0 + (uintptr_t)abytes;
+}
+
+}  // namespace
+
+extern "C" {
+
+int mamba_split_tf32(const float* x, int64_t rows, int64_t cols, int64_t ldx, int transpose,
+                     float* hi, float* lo, int64_t ld, void* stream) {
+  using mamba_scan::set_last_error;
+  if (rows < 0 || cols < 0 || ld < cols)
+    return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "split_tf32: bad sizes");
+  if (rows == 0 || cols == 0) return MAMBA_SCAN_OK;
+  if (!x || !hi || !lo)
+    return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "split_tf32: NULL pointer");
+  if (transpose ? ldx < rows : ldx < cols)
+    return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "split_tf32: ldx too small");
+  if (rows > ((int64_t)1 << 31) || cols > ((int64_t)1 << 31) ||
+      (!transpose && rows * cols > ((int64_t)1 << 40)))
+    return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "split_tf32: too large");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (transpose) {
+    const dim3 grid((unsigned)((rows + 31) / 32), (unsigned)((cols + 31) / 32));
+    if (grid.y > 65535)
+      return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "split_tf32: too many columns");
+    mamba_gemm::split_transpose_kernel<<<grid, dim3(32, 8), 0, st>>>(x, (int)rows, (int)cols,
+                                                                     ldx, hi, lo, ld);
+  } else {
+    const bool vec = al16(x) && al16(hi) && al16(lo) && ldx % 4 == 0 && ld % 4 == 0;
+    for (int64_t r0 = 0; r0 < rows; r0 += 65535) {  // grid.y holds at most 65535 rows
+      const dim3 grid((unsigned)((cols + 4 * 128 - 1) / (4 * 128)),
+                      (unsigned)std::min<int64_t>(65535, rows - r0));
+      mamba_gemm::split_rows_kernel<<<grid, 128, 0, st>>>(x + r0 * ldx, (int)cols, ldx,
+                                                          hi + r0 * ld, lo + r0 * ld, ld, vec);
+    }
+  }
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_last_error(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
+  return MAMBA_SCAN_OK;
+}
+
+int mamba_gemm_tf32x3(const float* a_hi, const float* a_lo, int64_t lda, const float* b_hi,
+                      const float* b_lo, int64_t ldb, const float* c_in, float* c,
+                      int64_t ldc_m, int64_t ldc_n, int64_t M, int64_t N, int64_t K,
+                      void* stream) {
+  using mamba_scan::set_last_error;
+  if (M < 0 || N < 0 || K < 0)
+    return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "gemm_tf32x3: negative size");
+  if (M == 0 || N == 0) return MAMBA_SCAN_OK;
+  if (K == 0)
+    return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "gemm_tf32x3: K must be positive");
+  if (M > ((int64_t)1 << 30) || N > ((int64_t)1 << 30) || K > ((int64_t)1 << 30))
+    return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "gemm_tf32x3: size exceeds 2^30");
+  if (!a_hi || !a_lo || !b_hi || !b_lo || !c)
+    return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "gemm_tf32x3: NULL pointer");
+  if (lda < K || ldb < K || lda % 4 != 0 || ldb % 4 != 0)
+    return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT,
+                          "gemm_tf32x3: lda and ldb must be >= K and multiples of 4");
+  if (!al16(a_hi) || !al16(a_lo) || !al16(b_hi) || !al16(b_lo))
+    return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT,
+                          "gemm_tf32x3: operands must be 16-byte aligned");
+  if (ldc_m <= 0 || ldc_n <= 0)
+    return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "gemm_tf32x3: C strides must be positive");
+  // C is written while the operands are read by other CTAs: no overlap.
+  const int64_t c_bytes = ((M - 1) * ldc_m + (N - 1) * ldc_n + 1) * 4;
+  const int64_t a_bytes = ((M - 1) * lda + K) * 4, b_bytes = ((N - 1) * ldb + K) * 4;
+  const void* ops[4] = {a_hi, a_lo, b_hi, b_lo};
+  const int64_t op_bytes[4] = {a_bytes, a_bytes, b_bytes, b_bytes};
+  for (int i = 0; i < 4; ++i)
+    if (overlap(c, c_bytes, ops[i], op_bytes[i]) ||
+        (c_in && overlap(c_in, c_bytes, ops[i], op_bytes[i])))
+      return set_last_error(MAMBA_SCAN_ERR_ALIASING, "gemm_tf32x3: C overlaps an operand");
+  if (c_in && c_in != c && overlap(c_in, c_bytes, c, c_bytes))
+    return set_last_error(MAMBA_SCAN_ERR_ALIASING,
+                          "gemm_tf32x3: c_in must be C itself or not overlap it");
+  const int64_t n_tiles = (N + mamba_gemm::BN - 1) / mamba_gemm::BN;
+  const int64_t m_tiles = (M + mamba_gemm::BM - 1) / mamba_gemm::BM;
+  if (m_tiles > 0x7FFFFFFF || n_tiles > 65535)
+    return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "gemm_tf32x3: too many tiles");
+  auto enc = gemm_encode_fn();
+  mamba_gemm::GemmMaps maps;
+  std::memset(&maps, 0, sizeof maps);
+  if (!enc || !encode_operand(enc, &maps.a_hi, a_hi, M, K, lda) ||
+      !encode_operand(enc, &maps.a_lo, a_lo, M, K, lda) ||
+      !encode_operand(enc, &maps.b_hi, b_hi, N, K, ldb) ||
+      !encode_operand(enc, &maps.b_lo, b_lo, N, K, ldb))
+    return set_last_error(MAMBA_SCAN_ERR_CUDA, "gemm_tf32x3: tensor map encoding failed");
+  static std::once_flag attr_once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(attr_once, [] {
+    attr_err = cudaFuncSetAttribute(mamba_gemm::gemm_tf32x3_kernel,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)mamba_gemm::kSmemBytes);
+  });
+  if (attr_err != cudaSuccess)
+    return set_last_error(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(attr_err));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  mamba_gemm::GemmParams p{c, c_in, ldc_m, ldc_n, (int)M, (int)N, (int)K};
+  mamba_gemm::gemm_tf32x3_kernel<<<dim3((unsigned)m_tiles, (unsigned)n_tiles),
+                                   mamba_gemm::kThreads,
+                                   mamba_gemm::kSmemBytes, st>>>(maps, p);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_last_error(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
+  return MAMBA_SCAN_OK;
+}
+
+}  // extern "C"

@@ -341,7 +341,10 @@ int mamba_scan_check_device_error(void) {
   int code = 0;
   const cudaError_t e = mamba_scan::read_and_clear_device_error(&code);
   if (e != cudaSuccess) return fail(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
-  return code;
+  // the model-ops GEMM keeps its own word (same codes)
+  const int g = mamba_gemm::read_and_clear_error();
+  if (g < 0) return fail(MAMBA_SCAN_ERR_CUDA, "cannot read the GEMM error word");
+  return code != 0 ? code : g;
 }
 
 int mamba_scan_selftest_wait_timeout(int64_t limit_ns, void* stream) {

@@ -75,3 +75,9 @@ int set_last_error(int status, const std::string& msg);
 cudaError_t read_and_clear_device_error(int* code);
 
 }  // namespace mamba_scan
+
+namespace mamba_gemm {
+// The tensor-core GEMM's own error word (a bounded wait that gave up): its
+// code, or -1 when it cannot be read; cleared when set.
+int read_and_clear_error();
+}  // namespace mamba_gemm

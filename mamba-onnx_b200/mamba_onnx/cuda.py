@@ -80,6 +80,12 @@ def library() -> ctypes.CDLL:
         lib.mamba_causal_conv1d_silu.restype = ctypes.c_int
         lib.mamba_causal_conv1d_silu.argtypes = [ctypes.c_void_p, ctypes.c_int64] + \
             [ctypes.c_void_p] * 3 + [ctypes.c_int64] * 4 + [ctypes.c_void_p]
+        lib.mamba_split_tf32.restype = ctypes.c_int
+        lib.mamba_split_tf32.argtypes = [ctypes.c_void_p] + [ctypes.c_int64] * 3 + \
+            [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p]
+        lib.mamba_gemm_tf32x3.restype = ctypes.c_int
+        lib.mamba_gemm_tf32x3.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64] * 2 + \
+            [ctypes.c_void_p] * 2 + [ctypes.c_int64] * 5 + [ctypes.c_void_p]
         _lib = lib
     return _lib
 
@@ -247,3 +253,71 @@ def causal_conv1d_silu(x, weight, bias=None, out=None, stream=None):
     if rc != STATUS_OK:
         _raise(rc, "causal_conv1d_silu")
     return out
+
+
+class SplitTF32:
+    """An fp32 matrix [rows][cols] as two tf32 parts (hi = tf32(x), lo =
+    tf32(x - hi)), rows padded to a multiple of 4 floats: the operand form of
+    gemm_tf32x3. Built by split_tf32."""
+
+    def __init__(self, hi, lo, rows: int, cols: int):
+        self.hi, self.lo, self.rows, self.cols = hi, lo, rows, cols
+
+    @property
+    def ld(self) -> int:
+        return self.hi.shape[1]
+
+
+def split_tf32(x, transpose: bool = False, out: SplitTF32 | None = None,
+               stream=None) -> SplitTF32:
+    """Split a 2-D CUDA float32 matrix (rows contiguous, any row stride) into
+    its tf32 parts; ``transpose`` splits x.t() instead (x [cols][rows])."""
+    import torch
+
+    if x.dim() != 2 or not x.is_cuda or x.dtype != torch.float32:
+        raise TypeError("x must be a 2-D CUDA float32 tensor")
+    if x.shape[1] > 1 and x.stride(1) != 1:
+        raise ValueError("x rows must be contiguous")
+    rows, cols = (x.shape[1], x.shape[0]) if transpose else (x.shape[0], x.shape[1])
+    ldx = x.stride(0) if x.shape[0] > 1 else x.shape[1]
+    ld = (cols + 3) // 4 * 4
+    if out is None:
+        out = SplitTF32(torch.empty((rows, ld), dtype=torch.float32, device=x.device),
+                        torch.empty((rows, ld), dtype=torch.float32, device=x.device), rows, cols)
+    elif (out.rows, out.cols) != (rows, cols):
+        raise ValueError("out has the wrong shape")
+    st = stream if stream is not None else torch.cuda.current_stream(x.device)
+    rc = library().mamba_split_tf32(_ptr(x), rows, cols, ldx, int(transpose), _ptr(out.hi),
+                                    _ptr(out.lo), out.ld, st.cuda_stream)
+    if rc != STATUS_OK:
+        _raise(rc, "split_tf32")
+    return out
+
+
+def gemm_tf32x3(a: SplitTF32, b: SplitTF32, c, *, transpose_c: bool = False,
+                c_in=None, stream=None):
+    """c = (c_in +) a @ b.T on the tensor cores, fp32-accurate (3xTF32): a
+    [M][K], b [N][K] split operands; c a CUDA float32 tensor viewed as [M, N]
+    (or, with ``transpose_c``, as [N, M]: c[n][m] receives element (m, n));
+    c_in None or a tensor with c's shape and strides (c itself allowed).
+    Returns c."""
+    import torch
+
+    if a.cols != b.cols:
+        raise ValueError(f"inner sizes differ: {a.cols} vs {b.cols}")
+    M, N, K = a.rows, b.rows, a.cols
+    if c.dim() != 2 or not c.is_cuda or c.dtype != torch.float32:
+        raise TypeError("c must be a 2-D CUDA float32 tensor")
+    if tuple(c.shape) != ((N, M) if transpose_c else (M, N)):
+        raise ValueError(f"c must be {(N, M) if transpose_c else (M, N)}, got {tuple(c.shape)}")
+    s0, s1 = c.stride()
+    ldc_m, ldc_n = (s1, s0) if transpose_c else (s0, s1)
+    if c_in is not None and (c_in.shape != c.shape or c_in.stride() != c.stride()
+                             or not c_in.is_cuda or c_in.dtype != torch.float32):
+        raise ValueError("c_in must be a CUDA float32 tensor with c's shape and strides")
+    st = stream if stream is not None else torch.cuda.current_stream(c.device)
+    rc = library().mamba_gemm_tf32x3(_ptr(a.hi), _ptr(a.lo), a.ld, _ptr(b.hi), _ptr(b.lo), b.ld,
+                                     _ptr(c_in), _ptr(c), ldc_m, ldc_n, M, N, K, st.cuda_stream)
+    if rc != STATUS_OK:
+        _raise(rc, "gemm_tf32x3")
+    return c

@@ -11,7 +11,12 @@ exp(delta*A), softplus(delta + dt_proj.bias) fused into the op through its
 ``MambaForCausalLM`` so its weights load directly; its ``MambaMixer.slow_forward``
 is the numerical reference.
 
-Everything is float32. ``forward`` runs a whole sequence; ``step`` decodes one
+Everything is float32. On CUDA the large projections (in_proj, out_proj and
+the LM head) over 16 or more tokens run on this package's tensor-core GEMM in
+3xTF32 form (operands split into two tf32 parts, three products summed with
+fp32 accumulation: fp32-accurate; ``GEMM = "cublas"`` selects torch's fp32
+GEMMs instead); x_proj and dt_proj (too few output tiles to fill the GPU)
+and single-token steps use torch's fp32 GEMMs. ``forward`` runs a whole sequence; ``step`` decodes one
 token from a ``DecodeState`` (the convolution window and the 16 scan states
 per channel), which the scan carries in through ``h0`` and out through
 ``h_last``. On CUDA tensors the RMSNorms and the causal convolution + SiLU run
@@ -68,9 +73,40 @@ def conv_silu(x, weight, bias):
     return F.silu(F.conv1d(x, weight, bias, padding=K - 1, groups=x.shape[1])[..., :L])
 
 
-def add_out_proj(h, y, weight):
-    """h + y^T W^T for h [B, L, d], y [B, D, L]; with one batch entry the sum is
-    the GEMM's own accumulation (addmm), not a separate kernel."""
+# Dense projections of at least this many tokens run on the tensor-core
+# 3xTF32 GEMM (cuda.gemm_tf32x3, fp32-accurate) when GEMM == "tf32x3"; fewer
+# tokens (decoding) and GEMM == "cublas" use torch's fp32 GEMMs (TF32 off).
+GEMM = "tf32x3"
+TC_MIN_TOKENS = 16
+
+
+def _use_tc(x, tokens: int) -> bool:
+    return x.is_cuda and GEMM == "tf32x3" and tokens >= TC_MIN_TOKENS
+
+
+class _SplitWeight:
+    """A weight's tf32 split (cuda.split_tf32), redone when the weight changes."""
+
+    def __init__(self):
+        self.key, self.split = None, None
+
+    def get(self, w):
+        key = (w.data_ptr(), w._version, tuple(w.shape))
+        if self.key != key:
+            self.split, self.key = cuda.split_tf32(w.detach()), key
+        return self.split
+
+
+def add_out_proj(h, y, weight, split=None):
+    """h + y^T W^T for h [B, L, d], y [B, D, L]; the sum is the GEMM's own
+    accumulation (addmm, or the tensor-core GEMM's c_in), not a separate kernel."""
+    if split is not None and _use_tc(h, h.shape[1]):
+        w = split.get(weight)
+        out = torch.empty_like(h)
+        for b in range(h.shape[0]):  # out[b] [L, d] = h[b] + (y[b]^T [L, D]) W^T
+            cuda.gemm_tf32x3(w, cuda.split_tf32(y[b], transpose=True), out[b],
+                             transpose_c=True, c_in=h[b])
+        return out
     if h.shape[0] == 1:
         return torch.addmm(h[0], y[0].t(), weight.t()).unsqueeze(0)
     return h + torch.matmul(y.transpose(1, 2), weight.t())
@@ -99,6 +135,16 @@ class MambaLayer(torch.nn.Module):
         self.A_log = torch.nn.Parameter(torch.empty(D, N, **f32))
         self.D = torch.nn.Parameter(torch.ones(D, **f32))
         self.out_proj_weight = torch.nn.Parameter(torch.empty(d, D, **f32))
+        self._in_split, self._out_split = _SplitWeight(), _SplitWeight()
+        self._A_key, self._A = None, None
+
+    def A(self):
+        """-exp(A_log), recomputed only when A_log changes."""
+        key = (self.A_log.data_ptr(), self.A_log._version, self.A_log.device)
+        if self._A_key != key:
+            with torch.no_grad():
+                self._A, self._A_key = -torch.exp(self.A_log), key
+        return self._A
 
     def _norm(self, x):
         return rms_norm(x, self.norm_weight, self.cfg.rms_eps)
@@ -119,6 +165,12 @@ class MambaLayer(torch.nn.Module):
     def _in_proj(self, h):
         """rmsnorm(h) [B, L, d] -> in_proj output xz [B, 2D, L] (x rows, then z rows)."""
         hn = self._norm(h)
+        if _use_tc(h, h.shape[1]):
+            w = self._in_split.get(self.in_proj_weight)
+            xz = torch.empty(h.shape[0], w.rows, h.shape[1], device=h.device)
+            for b in range(h.shape[0]):  # xz[b] [2D, L] = W hn[b]^T
+                cuda.gemm_tf32x3(w, cuda.split_tf32(hn[b]), xz[b])
+            return xz
         if h.shape[0] == 1:
             return torch.mm(self.in_proj_weight, hn[0].t()).unsqueeze(0)
         return torch.matmul(self.in_proj_weight, hn.transpose(1, 2))
@@ -138,7 +190,7 @@ class MambaLayer(torch.nn.Module):
                  h_last=ssm_state)
         if conv_state is not None:  # the last K inputs of the convolution, zero-padded
             conv_state.copy_(F.pad(xz[:, :D], (max(0, K - L), 0))[..., -K:])
-        return add_out_proj(h, y, self.out_proj_weight)
+        return add_out_proj(h, y, self.out_proj_weight, self._out_split)
 
     def step(self, h, A, conv_state, ssm_state):
         """One token: h [B, 1, d_model]; conv_state [B, D, d_conv] (last inputs of
@@ -172,6 +224,7 @@ class MambaLM(torch.nn.Module):
         self.embedding = torch.nn.Parameter(torch.empty(cfg.vocab_size, cfg.d_model))
         self.layers = torch.nn.ModuleList(MambaLayer(cfg) for _ in range(cfg.n_layer))
         self.norm_f_weight = torch.nn.Parameter(torch.ones(cfg.d_model))
+        self._emb_split = _SplitWeight()
 
     # ---------------------------------------------------------------- weights
 
@@ -226,6 +279,12 @@ class MambaLM(torch.nn.Module):
 
     def _head(self, h):
         h = rms_norm(h, self.norm_f_weight, self.cfg.rms_eps)
+        if _use_tc(h, h.shape[1]):
+            e = self._emb_split.get(self.embedding)
+            logits = torch.empty(h.shape[0], h.shape[1], e.rows, device=h.device)
+            for b in range(h.shape[0]):  # logits[b] [L, V] = h[b] E^T
+                cuda.gemm_tf32x3(cuda.split_tf32(h[b]), e, logits[b])
+            return logits
         return torch.matmul(h, self.embedding.t())
 
     @torch.no_grad()
@@ -235,7 +294,7 @@ class MambaLM(torch.nn.Module):
         default the scans run on cuda.selective_scan and need a CUDA device."""
         h = F.embedding(input_ids, self.embedding)
         for layer in self.layers:
-            h = layer(h, -torch.exp(layer.A_log), scan=scan)
+            h = layer(h, layer.A(), scan=scan)
         return self._head(h)
 
     @torch.no_grad()
@@ -244,7 +303,7 @@ class MambaLM(torch.nn.Module):
         state = self.new_state(input_ids.shape[0])
         h = F.embedding(input_ids, self.embedding)
         for layer, cs, ss in zip(self.layers, state.conv, state.ssm):
-            h = layer(h, -torch.exp(layer.A_log), cs, ss)
+            h = layer(h, layer.A(), cs, ss)
         return self._head(h), state
 
     def new_state(self, batch: int) -> DecodeState:
@@ -258,7 +317,7 @@ class MambaLM(torch.nn.Module):
         """One decoding step: input_ids [B] -> logits [B, vocab]; state updated."""
         h = F.embedding(input_ids[:, None], self.embedding)
         for layer, cs, ss in zip(self.layers, state.conv, state.ssm):
-            h = layer.step(h, -torch.exp(layer.A_log), cs, ss)
+            h = layer.step(h, layer.A(), cs, ss)
         return self._head(h)[:, 0]
 
     @torch.no_grad()

@@ -115,6 +115,31 @@ def test_model_kernels_validate_before_launch():
                                         None) == 0  # empty
 
 
+def test_gemm_and_split_validate_before_launch():
+    """mamba_split_tf32 / mamba_gemm_tf32x3 reject bad arguments without CUDA."""
+    lib = cuda.library()
+    f = 0x100000  # 16-byte aligned fake device addresses, 1 MiB apart
+    # split: ld >= cols, ldx >= cols (rows when transposing), no NULLs; empty is a no-op
+    assert lib.mamba_split_tf32(f, 4, 8, 8, 0, 2 * f, 3 * f, 7, None) == 1
+    assert lib.mamba_split_tf32(f, 4, 8, 7, 0, 2 * f, 3 * f, 8, None) == 1
+    assert lib.mamba_split_tf32(f, 4, 8, 3, 1, 2 * f, 3 * f, 8, None) == 1
+    assert lib.mamba_split_tf32(None, 4, 8, 8, 0, 2 * f, 3 * f, 8, None) == 1
+    assert lib.mamba_split_tf32(f, 0, 8, 8, 0, 2 * f, 3 * f, 8, None) == 0
+
+    def gemm(a_hi=f, a_lo=2 * f, lda=16, b_hi=3 * f, b_lo=4 * f, ldb=16, c_in=None, c=5 * f,
+             ldc_m=8, ldc_n=1, M=4, N=8, K=16):
+        return lib.mamba_gemm_tf32x3(a_hi, a_lo, lda, b_hi, b_lo, ldb, c_in, c, ldc_m, ldc_n,
+                                     M, N, K, None)
+
+    assert gemm(K=0) == 1
+    assert gemm(M=0) == 0 and gemm(N=0) == 0  # empty product
+    assert gemm(lda=12) == 1 and gemm(ldb=18) == 1  # < K / not a multiple of 4
+    assert gemm(b_lo=4 * f + 8) == 1 and b"aligned" in lib.mamba_scan_last_error()
+    assert gemm(c=f + 64) == 4 and b"overlaps" in lib.mamba_scan_last_error()
+    assert gemm(c_in=5 * f + 16) == 4  # partly overlapping C
+    assert gemm(ldc_m=0) == 1
+
+
 def test_empty_batch_is_a_no_op():
     lib = cuda.library()
     assert lib.mamba_scan_launch(0, ctypes.byref(_args(batch=0)), None, 0, None) == 0
