@@ -252,6 +252,9 @@ def main():
                          "distributions; non-fused ops draw delta per element)")
     ap.add_argument("--workload", choices=["scan", "scan-b64", "mamba130m", "mamba130m-decode"],
                     default="scan")
+    ap.add_argument("--gemm-case", default=None, metavar="M:N:K",
+                    help="profiling helper: warmup + steps calls of the tensor-core 3xTF32 "
+                         "GEMM on random [M,K] x [N,K] operands; nothing timed")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.workload == "mamba130m":
@@ -262,6 +265,8 @@ def main():
         return run_scan_b64(args)
     if args.ncu_case and args.case:
         return run_case(args)
+    if args.gemm_case:
+        return run_gemm_case(args)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -675,6 +680,24 @@ def run_case(args):
     torch.cuda.synchronize()
     print(json.dumps({"ncu_case": args.case, "launches_per_call": 3 if ws_bytes else 1,
                       "calls": args.warmup + args.steps}))
+
+
+def run_gemm_case(args):
+    """Profiling helper: warmup + steps calls of gemm_tf32x3 on one shape, nothing timed."""
+    import torch
+
+    from mamba_onnx import cuda
+
+    M, N, K = (int(v) for v in args.gemm_case.split(":"))
+    device = torch.device("cuda", 0)
+    g = torch.Generator(device=device).manual_seed(SEED)
+    a = cuda.split_tf32(torch.randn(M, K, device=device, generator=g))
+    b = cuda.split_tf32(torch.randn(N, K, device=device, generator=g))
+    c = torch.empty(M, N, device=device)
+    for _ in range(args.warmup + args.steps):
+        cuda.gemm_tf32x3(a, b, c)
+    torch.cuda.synchronize()
+    print(json.dumps({"gemm_case": args.gemm_case, "calls": args.warmup + args.steps}))
 
 
 B64_BATCH, B64_SEQLEN, B64_SEED = 64, 4096, 3
