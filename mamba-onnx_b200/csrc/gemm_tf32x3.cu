@@ -11,22 +11,23 @@
 // rounding of the lo parts), the same order as the fp32 rounding of the
 // accumulation itself.
 //
-// One CTA = one 128 x 128 output tile, 10 warps:
-// * warp 8 lane 0 (producer) streams 32-wide K blocks of A_hi, A_lo, B_hi,
-//   B_lo by TMA (128-byte swizzle, 4 x 16 KB per stage, 3-stage ring);
-// * warp 9 lane 0 (MMA issuer) waits for a stage, issues 4 K-steps x 3
-//   products of tcgen05.mma.kind::tf32 (M = 128, N = 128, K = 8) into a
+// One CTA = one 128 x BN output tile (BN = 128 or 192), 10 or 14 warps:
+// * the producer warp's lane 0 streams 32-wide K blocks of A_hi, A_lo,
+//   B_hi, B_lo by TMA (128-byte swizzle, 3 or 2 stages);
+// * the MMA warp's lane 0 waits for a stage, issues 4 K-steps x 3
+//   products of tcgen05.mma.kind::tf32 (M = 128, N = BN, K = 8) into a
 //   TMEM accumulator that starts from zero for every K block (corrections
 //   first, then hi*hi), and commits the stage back to the producer and the
 //   accumulator to the accumulator warps (two accumulators alternate);
-// * warps 0..7 (warp w owns TMEM lanes 32(w%4)..+31 = tile rows, and half
-//   of the columns) read each K block's sums (tcgen05.ld) and add them to
+// * 8 or 12 accumulator warps (warp w owns TMEM lanes 32(w%4)..+31 = tile
+//   rows, and 64 columns) read each K block's sums (tcgen05.ld), add them to
 //   fp32 registers, then store C with arbitrary strides, optionally adding
 //   a second matrix C_in (which may be C itself).
 // Every mbarrier wait is bounded (mamba_gemm error word on timeout).
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -40,18 +41,18 @@ namespace mamba_gemm {
 
 using mamba_scan::smem_u32;
 
-constexpr int BM = 128, BN = 128, BK = 32;  // BK fp32 = 128 bytes: one swizzled row
-constexpr int kStages = 3;
-// warps 0..7 accumulate and store: warp w owns TMEM lanes 32(w%4)..+31
-// (tile rows) and columns [64(w/4), 64(w/4) + 64), so two warps share each
-// SM sub-partition and hide each other's TMEM load latency
-constexpr int kAccWarps = 8;
-constexpr int kAccThreads = 32 * kAccWarps;
-constexpr int kAccCols = BN * 4 / kAccWarps;  // 64
-constexpr int kProducerWarp = kAccWarps, kMmaWarp = kAccWarps + 1;
-constexpr int kThreads = 32 * (kAccWarps + 2);
-constexpr uint32_t kTileBytes = BM * BK * 4;  // 16 KB (BN == BM)
-constexpr uint32_t kStageBytes = 4 * kTileBytes;
+constexpr int BM = 128, BK = 32;  // BK fp32 = 128 bytes: one swizzled row
+
+// Tile configurations: 128 x 128 with a 3-stage ring (64 KB per stage), or
+// 128 x 192 with 2 stages (80 KB per stage) for outputs whose 128-wide tiles
+// would leave a small last wave (the in_proj shape: 192 tiles on 148 SMs,
+// against 144 tiles of 192 columns).
+//
+// Warps 0..kAccWarps-1 accumulate and store: warp w owns TMEM lanes
+// 32(w%4)..+31 (tile rows) and columns [64(w/4), 64(w/4) + 64), so two or
+// three warps share each SM sub-partition and hide each other's TMEM load
+// latency; then one TMA producer warp and one MMA warp.
+//
 // Two fp32 accumulators of BN columns (alternate K blocks). The tensor
 // core's accumulation into TMEM loses accuracy with every update (on K =
 // 1536 one accumulator over the whole K ended 5x further from float64 than
@@ -60,20 +61,33 @@ constexpr uint32_t kStageBytes = 4 * kTileBytes;
 // 8 correction products (~2^-11 of the sums) go first, while the
 // accumulator is small, then the 4 hi*hi products: the corrections' own
 // rounding stays at their scale.
-constexpr int kTmemCols = 2 * BN;
-
-struct __align__(1024) GemmSmem {
-  float a_hi[kStages][BM * BK];
-  float a_lo[kStages][BM * BK];
-  float b_hi[kStages][BN * BK];
-  float b_lo[kStages][BN * BK];
-  uint64_t full[kStages];
-  uint64_t empty[kStages];
-  uint64_t acc_full[2];   // a K block's sums are in TMEM buffer b (tcgen05.commit)
-  uint64_t acc_empty[2];  // the accumulator warps have read buffer b
-  uint32_t tmem_base;
+template <int BN_, int kStages_>
+struct Cfg {
+  static constexpr int BN = BN_, kStages = kStages_;
+  static constexpr int kAccCols = 64;  // running sums per accumulator thread
+  static constexpr int kAccWarps = 4 * BN / kAccCols;
+  static constexpr int kAccThreads = 32 * kAccWarps;
+  static constexpr int kProducerWarp = kAccWarps, kMmaWarp = kAccWarps + 1;
+  static constexpr int kThreads = 32 * (kAccWarps + 2);
+  static constexpr uint32_t kATile = BM * BK * 4, kBTile = BN * BK * 4;
+  static constexpr uint32_t kStageBytes = 2 * kATile + 2 * kBTile;
+  static constexpr int kTmemCols = (2 * BN <= 256) ? 256 : 512;  // a power of two >= 2 BN
+  struct __align__(1024) Smem {
+    float a_hi[kStages][BM * BK];
+    float a_lo[kStages][BM * BK];
+    float b_hi[kStages][BN * BK];
+    float b_lo[kStages][BN * BK];
+    uint64_t full[kStages];
+    uint64_t empty[kStages];
+    uint64_t acc_full[2];   // a K block's sums are in TMEM accumulator b (tcgen05.commit)
+    uint64_t acc_empty[2];  // the accumulator warps have read accumulator b
+    uint32_t tmem_base;
+  };
+  static constexpr size_t kSmemBytes = sizeof(Smem) + 1024;  // + room to align the base
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
 };
-constexpr size_t kSmemBytes = sizeof(GemmSmem) + 1024;  // + room to align the base
+using Cfg128 = Cfg<128, 3>;
+using Cfg192 = Cfg<192, 2>;
 
 struct GemmMaps {
   CUtensorMap a_hi, a_lo, b_hi, b_lo;
@@ -125,11 +139,11 @@ __device__ __forceinline__ uint64_t sw128_desc(const void* tile) {
 
 // Instruction descriptor of kind::tf32, D = F32, A = B = TF32, both K-major,
 // N >> 3 in bits [17,23), M >> 4 in bits [24,29) (UMMA InstrDescriptor).
-constexpr uint32_t kInstrDesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) |
-                                ((uint32_t)(BM >> 4) << 24);
-
+template <int BN>
 __device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
                                          uint32_t accumulate) {
+  constexpr uint32_t kInstrDesc = (1u << 4) | (2u << 7) | (2u << 10) |
+                                  ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
   asm volatile(
       "{\n\t"
       ".reg .pred p;\n\t"
@@ -170,10 +184,13 @@ __device__ __forceinline__ void tmem_wait() {
 
 // ------------------------------------------------------------------ kernel
 
-__global__ void __launch_bounds__(kThreads, 1)
+template <class C>
+__global__ void __launch_bounds__(C::kThreads, 1)
     gemm_tf32x3_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
+  constexpr int BN = C::BN, kStages = C::kStages, kAccCols = C::kAccCols;
+  constexpr int kProducerWarp = C::kProducerWarp, kMmaWarp = C::kMmaWarp;
   extern __shared__ uint8_t smem_raw[];
-  GemmSmem& sm = *reinterpret_cast<GemmSmem*>(
+  typename C::Smem& sm = *reinterpret_cast<typename C::Smem*>(
       smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // M tiles vary fastest: the CTAs running together share B tiles (the
@@ -188,7 +205,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mamba_scan::mbar_init(&sm.acc_full[b], 1);
-      mamba_scan::mbar_init(&sm.acc_empty[b], kAccThreads);
+      mamba_scan::mbar_init(&sm.acc_empty[b], C::kAccThreads);
     }
     mamba_scan::fence_mbarrier_init();
   }
@@ -201,7 +218,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {  // the whole warp allocates the accumulators' TMEM columns
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(&sm.tmem_base)),
-                 "r"(kTmemCols)
+                 "r"(C::kTmemCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -218,7 +235,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             !mamba_scan::mbar_wait(&sm.empty[s], (uint32_t)((kb / kStages) - 1) & 1u,
                                    &g_gemm_device_error))
           break;
-        mamba_scan::mbar_arrive_expect_tx(&sm.full[s], kStageBytes);
+        mamba_scan::mbar_arrive_expect_tx(&sm.full[s], C::kStageBytes);
         const int k0 = kb * BK;
         tma_load_2d(sm.a_hi[s], &maps.a_hi, &sm.full[s], k0, m0);
         tma_load_2d(sm.a_lo[s], &maps.a_lo, &sm.full[s], k0, m0);
@@ -247,13 +264,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int k = 0; k < BK / 8; ++k) {
           const uint64_t off = (uint64_t)(k * 32) >> 4;  // 8 tf32 = 32 bytes along the row
-          mma_tf32(t, al + off, bh + off, k > 0 ? 1u : 0u);
-          mma_tf32(t, ah + off, bl + off, 1u);
+          mma_tf32<BN>(t, al + off, bh + off, k > 0 ? 1u : 0u);
+          mma_tf32<BN>(t, ah + off, bl + off, 1u);
         }
 #pragma unroll
         for (int k = 0; k < BK / 8; ++k) {
           const uint64_t off = (uint64_t)(k * 32) >> 4;
-          mma_tf32(t, ah + off, bh + off, 1u);
+          mma_tf32<BN>(t, ah + off, bh + off, 1u);
         }
         mma_commit(&sm.empty[s]);     // the stage is free once these MMAs have read it
         mma_commit(&sm.acc_full[b]);  // and the block's sums are ready
@@ -276,15 +293,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
       const uint32_t t = lane_base + (uint32_t)(b * BN);
-      uint32_t v[kAccCols];
+      // 64 columns per wait for the 128-column tile; 32 for the 192-column
+      // one, whose 14 warps leave 128 registers per thread
+      constexpr int kMax = (C::kThreads <= 320) ? 64 : 32;
 #pragma unroll
-      for (int c = 0; c < kAccCols; c += 32)
-        tmem_ld32(t + (uint32_t)c, *reinterpret_cast<uint32_t(*)[32]>(v + c));
-      tmem_wait();
+      for (int c0 = 0; c0 < kAccCols; c0 += kMax) {
+        uint32_t v[kMax];
 #pragma unroll
-      for (int j = 0; j < kAccCols / 2; ++j)
-        acc[j] = __fadd2_rn(acc[j], make_float2(__uint_as_float(v[2 * j]),
-                                                __uint_as_float(v[2 * j + 1])));
+        for (int c = 0; c < kMax; c += 32)
+          tmem_ld32(t + (uint32_t)(c0 + c), *reinterpret_cast<uint32_t(*)[32]>(v + c));
+        tmem_wait();
+#pragma unroll
+        for (int j = 0; j < kMax / 2; ++j)
+          acc[c0 / 2 + j] = __fadd2_rn(acc[c0 / 2 + j], make_float2(__uint_as_float(v[2 * j]),
+                                                                    __uint_as_float(v[2 * j + 1])));
+      }
       tc_fence_before();
       mbar_arrive(&sm.acc_empty[b]);
     }
@@ -306,7 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                 "r"(kTmemCols)
+                 "r"(C::kTmemCols)
                  : "memory");
   }
 }
@@ -405,12 +428,12 @@ PFN_cuTensorMapEncodeTiled_v12000 gemm_encode_fn() {
   return fn;
 }
 
-// [rows][K] fp32, row stride ld floats, boxes of 32 K x 128 rows, 128-byte swizzle.
+// [rows][K] fp32, row stride ld floats, boxes of 32 K x box_rows rows, 128-byte swizzle.
 bool encode_operand(PFN_cuTensorMapEncodeTiled_v12000 enc, CUtensorMap* m, const float* ptr,
-                    int64_t rows, int64_t K, int64_t ld) {
+                    int64_t rows, int64_t K, int64_t ld, int box_rows) {
   const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
-  const cuuint32_t box[2] = {mamba_gemm::BK, mamba_gemm::BM};
+  const cuuint32_t box[2] = {mamba_gemm::BK, (cuuint32_t)box_rows};
   const cuuint32_t estr[2] = {1, 1};
   return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(ptr), dims, strides, box,
              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -419,6 +442,46 @@ bool encode_operand(PFN_cuTensorMapEncodeTiled_v12000 enc, CUtensorMap* m, const
 }
 
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int device_sms() {
+  static std::atomic<int> cache[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  int v = cache[dev].load(std::memory_order_relaxed);
+  if (v > 0) return v;
+  if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0)
+    v = 148;
+  cache[dev].store(v, std::memory_order_relaxed);
+  return v;
+}
+
+// 192-column tiles when they take fewer waves x columns than 128-column ones
+// (one CTA per SM; a CTA's time grows with its tile's columns).
+bool use_wide_tiles(int64_t M, int64_t N, int sms) {
+  const int64_t m_tiles = (M + mamba_gemm::BM - 1) / mamba_gemm::BM;
+  auto cost = [&](int64_t bn) {
+    const int64_t tiles = m_tiles * ((N + bn - 1) / bn);
+    return (tiles + sms - 1) / sms * bn;
+  };
+  return cost(192) < cost(128);
+}
+
+template <class C>
+cudaError_t launch_gemm(const mamba_gemm::GemmMaps& maps, const mamba_gemm::GemmParams& p,
+                        int64_t m_tiles, cudaStream_t st) {
+  static std::once_flag attr_once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(attr_once, [] {
+    attr_err = cudaFuncSetAttribute(mamba_gemm::gemm_tf32x3_kernel<C>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)C::kSmemBytes);
+  });
+  if (attr_err != cudaSuccess) return attr_err;
+  const int64_t n_tiles = (p.N + C::BN - 1) / C::BN;
+  mamba_gemm::gemm_tf32x3_kernel<C><<<dim3((unsigned)m_tiles, (unsigned)n_tiles), C::kThreads,
+                                      C::kSmemBytes, st>>>(maps, p);
+  return cudaGetLastError();
+}
 
 bool overlap(const void* a, int64_t abytes, const void* b, int64_t bbytes) {
   const auto a0 = reinterpret_cast<uintptr_t>(a), b0 = reinterpret_cast<uintptr_t>(b);
@@ -497,33 +560,23 @@ int mamba_gemm_tf32x3(const float* a_hi, const float* a_lo, int64_t lda, const f
   if (c_in && c_in != c && overlap(c_in, c_bytes, c, c_bytes))
     return set_last_error(MAMBA_SCAN_ERR_ALIASING,
                           "gemm_tf32x3: c_in must be C itself or not overlap it");
-  const int64_t n_tiles = (N + mamba_gemm::BN - 1) / mamba_gemm::BN;
   const int64_t m_tiles = (M + mamba_gemm::BM - 1) / mamba_gemm::BM;
-  if (m_tiles > 0x7FFFFFFF || n_tiles > 65535)
+  if (m_tiles > 0x7FFFFFFF || (N + 127) / 128 > 65535)
     return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "gemm_tf32x3: too many tiles");
+  const bool wide = use_wide_tiles(M, N, device_sms());
+  const int bn = wide ? mamba_gemm::Cfg192::BN : mamba_gemm::Cfg128::BN;
   auto enc = gemm_encode_fn();
   mamba_gemm::GemmMaps maps;
   std::memset(&maps, 0, sizeof maps);
-  if (!enc || !encode_operand(enc, &maps.a_hi, a_hi, M, K, lda) ||
-      !encode_operand(enc, &maps.a_lo, a_lo, M, K, lda) ||
-      !encode_operand(enc, &maps.b_hi, b_hi, N, K, ldb) ||
-      !encode_operand(enc, &maps.b_lo, b_lo, N, K, ldb))
+  if (!enc || !encode_operand(enc, &maps.a_hi, a_hi, M, K, lda, mamba_gemm::BM) ||
+      !encode_operand(enc, &maps.a_lo, a_lo, M, K, lda, mamba_gemm::BM) ||
+      !encode_operand(enc, &maps.b_hi, b_hi, N, K, ldb, bn) ||
+      !encode_operand(enc, &maps.b_lo, b_lo, N, K, ldb, bn))
     return set_last_error(MAMBA_SCAN_ERR_CUDA, "gemm_tf32x3: tensor map encoding failed");
-  static std::once_flag attr_once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(attr_once, [] {
-    attr_err = cudaFuncSetAttribute(mamba_gemm::gemm_tf32x3_kernel,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    (int)mamba_gemm::kSmemBytes);
-  });
-  if (attr_err != cudaSuccess)
-    return set_last_error(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(attr_err));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   mamba_gemm::GemmParams p{c, c_in, ldc_m, ldc_n, (int)M, (int)N, (int)K};
-  mamba_gemm::gemm_tf32x3_kernel<<<dim3((unsigned)m_tiles, (unsigned)n_tiles),
-                                   mamba_gemm::kThreads,
-                                   mamba_gemm::kSmemBytes, st>>>(maps, p);
-  const cudaError_t e = cudaGetLastError();
+  const cudaError_t e = wide ? launch_gemm<mamba_gemm::Cfg192>(maps, p, m_tiles, st)
+                             : launch_gemm<mamba_gemm::Cfg128>(maps, p, m_tiles, st);
   if (e != cudaSuccess) return set_last_error(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
   return MAMBA_SCAN_OK;
 }

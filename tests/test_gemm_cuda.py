@@ -47,6 +47,9 @@ CASES = [
     (3072, 1024, 768, False, False),    # in_proj: W [2D, d] x hn^T
     (768, 1024, 1536, True, True),      # out_proj into the residual [L, d]
     (1024, 2000, 768, False, False),    # an LM-head slice
+    # 192-column tiles (chosen when they take fewer waves): ragged M, N, K
+    (3000, 1000, 100, False, False),
+    (2900, 900, 40, True, True),
 ]
 
 
