@@ -446,7 +446,8 @@ MODEL_METRIC, MODEL_UNIT = "Mamba-130m forward tokens/s", "tokens/s"
 MODEL_WORKLOAD = ("Mamba-130m forward (24 blocks, d_model 768, d_inner 1536, d_state 16, "
                   "vocab 50280), fp32, batch 1 x seqlen 1024 per GPU, every selective scan on "
                   "SelectiveScanFusedExact; in_proj, out_proj and the LM head on the "
-                  "tensor-core 3xTF32 GEMM (fp32-accurate), x_proj and dt_proj on cuBLAS fp32")
+                  "tensor-core 3xTF32 GEMM (fp32-accurate), x_proj on this package's fp32 "
+                  "kernel, dt_proj on cuBLAS fp32")
 
 
 def model_cpu_sample(n_threads, budget_s=30.0):
@@ -630,9 +631,10 @@ def run_model(args):
                     "d2h_bytes_per_step": host_last.numel() * 4, "ms_per_step": e2e_ms,
                     "path": "pinned token ids -> graph replay -> last-position logits to host"},
             # this package's kernels per forward: per block RMSNorm, conv +
-            # SiLU, two tf32 splits and two GEMMs (in_proj, out_proj) and the
-            # scan; then the final RMSNorm, its split and the LM-head GEMM
-            "gpu_launches": (model.cfg.n_layer * (6 + launches_per_scan) + 3) * args.steps,
+            # SiLU, x_proj, two tf32 splits and two GEMMs (in_proj, out_proj)
+            # and the scan; then the final RMSNorm, its split and the LM-head
+            # GEMM
+            "gpu_launches": (model.cfg.n_layer * (7 + launches_per_scan) + 3) * args.steps,
             "scan_ms_per_step": scan_ms,
             "roofline": {"bound": "hbm", "kernel": f"the {model.cfg.n_layer} {SCAN_OP} calls of "
                          f"one forward (1x{D}x{L} each)", "achieved": achieved, "peak": hbm_peak,

@@ -48,6 +48,20 @@ MAMBA_SCAN_API int mamba_causal_conv1d_silu(const float* x, int64_t x_batch_stri
                                             int64_t width, void* stream);
 
 /*
+ * Mamba's x_proj for every token, split into the scan's inputs:
+ *   [dt | B | C][b, t, :] = weight . x[b, :, t]
+ * x is [batch][dim][seqlen] contiguous (the convolution output, channel
+ * rows), weight is x_proj's [rank + 2*dstate][dim]; the first `rank` outputs
+ * go to dt [batch][seqlen][rank], the next `dstate` to B and the last
+ * `dstate` to C ([batch][seqlen][dstate] each, the scan op's B/C layout).
+ * fp32 throughout, deterministic; rank + 2*dstate <= 128. No output may
+ * overlap an input or another output.
+ */
+MAMBA_SCAN_API int mamba_x_proj(const float* x, const float* weight, float* dt, float* B, float* C,
+                                int64_t batch, int64_t dim, int64_t seqlen, int64_t rank,
+                                int64_t dstate, void* stream);
+
+/*
  * Split fp32 values into two tf32 parts for mamba_gemm_tf32x3:
  *   hi = tf32(x), lo = tf32(x - hi)   (round to nearest; x - hi is exact),
  * written as [rows][cols] with row stride `ld` (>= cols) into hi and lo.

@@ -12,16 +12,31 @@
 //   before t = 0 (torch's conv1d with padding K-1, sliced to the first L
 //   outputs): one thread per four consecutive steps of one channel.
 //
-// Both are memory-bound (two HBM passes over their tensor); the C entry
+// * x_proj, [dt | B | C][t] = W_x x[:, t], for every token: a thread-block
+//   cluster of 8 CTAs per 32 tokens, each CTA summing 1/8 of d_inner (in
+//   96-row steps) into a 32 x P partial tile in shared memory (4 tokens x
+//   P/32 outputs per thread in registers), then each CTA adds 4 token rows
+//   of all 8 partials in cluster-rank order through distributed shared
+//   memory (deterministic, no
+//   global scratch) and writes them straight into the three outputs the scan
+//   takes (dt [L][rank], B and C [L][dstate] contiguous);
+//
+// The first two are memory-bound (two HBM passes over their tensor); x_proj
+// replaces a cuBLAS fp32 GEMM that its skinny shape leaves at a few CTAs,
+// plus the copies of the B and C slices out of its output. The C entry
 // points are declared in include/mamba_model_ops.h.
+#include <cooperative_groups.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
 #include <string>
 
 #include "../../include/mamba_model_ops.h"
 #include "../../include/mamba_scan.h"
 #include "scan_kernels.h"
+
+namespace cg = cooperative_groups;
 
 namespace {
 
@@ -119,7 +134,128 @@ __global__ void __launch_bounds__(kConvThreads)
   }
 }
 
+// ------------------------------------------------------------------ x_proj
+
+constexpr int kXpCluster = 8;    // CTAs per token block, each 1/8 of d_inner
+constexpr int kXpTokens = 32;    // tokens per block: 8 groups of 4
+constexpr int kXpThreads = 256;  // 8 token groups x 32 output groups
+constexpr int kXpDChunk = 96;    // d_inner rows staged per step (2 steps at d_inner 1536)
+constexpr int kXpMaxOut = 128;   // rank + 2 * dstate
+constexpr int kXpRow = kXpMaxOut + 1;  // padded smem rows (conflict-free column writes)
+
+struct XpStage {
+  float x[kXpDChunk][kXpTokens];  // x[d][t] of the chunk
+  float w[kXpDChunk][kXpRow];     // W_x[j][d], transposed to [d][j]
+};
+union XpSmem {
+  XpStage stage;
+  float part[kXpTokens][kXpRow];  // this CTA's partial sums, [t][j]
+};
+constexpr size_t kXpSmemBytes = sizeof(XpSmem);
+
+// kOut = outputs per thread (P <= 32 kOut): 3 for Mamba-130m's P = 80.
+template <int kOut>
+__global__ void __cluster_dims__(kXpCluster, 1, 1) __launch_bounds__(kXpThreads)
+    xproj_kernel(const float* __restrict__ x, const float* __restrict__ w, float* __restrict__ dt,
+                 float* __restrict__ Bm, float* __restrict__ Cm, int dim, int seqlen, int rank,
+                 int dstate) {
+  extern __shared__ __align__(16) uint8_t xp_raw[];
+  XpSmem& sm = *reinterpret_cast<XpSmem*>(xp_raw);
+  cg::cluster_group cluster = cg::this_cluster();
+  const int crank = (int)cluster.block_rank();
+  const int b = blockIdx.y;
+  const int t0 = (blockIdx.x / kXpCluster) * kXpTokens;
+  const int P = rank + 2 * dstate;
+  const int per = (dim + kXpCluster - 1) / kXpCluster;
+  const int d_lo = min(dim, crank * per), d_hi = min(dim, d_lo + per);
+  const float* xb = x + (int64_t)b * dim * seqlen;
+  const int tid = threadIdx.x, tg = tid & 7, og = tid >> 3;
+
+  float acc[4][kOut];
+#pragma unroll
+  for (int a = 0; a < 4; ++a)
+#pragma unroll
+    for (int k = 0; k < kOut; ++k) acc[a][k] = 0.f;
+
+  for (int dc = d_lo; dc < d_hi; dc += kXpDChunk) {
+    __syncthreads();  // the previous chunk has been read
+    for (int i = tid; i < kXpDChunk * kXpTokens; i += kXpThreads) {
+      const int dd = i / kXpTokens, tt = i % kXpTokens;
+      const int d = dc + dd, t = t0 + tt;
+      sm.stage.x[dd][tt] = (d < d_hi && t < seqlen) ? __ldg(xb + (int64_t)d * seqlen + t) : 0.f;
+    }
+    for (int i = tid; i < P * kXpDChunk; i += kXpThreads) {
+      const int j = i / kXpDChunk, dd = i % kXpDChunk;
+      const int d = dc + dd;
+      sm.stage.w[dd][j] = (d < d_hi) ? __ldg(w + (int64_t)j * dim + d) : 0.f;
+    }
+    __syncthreads();
+    const int n = min(kXpDChunk, d_hi - dc);
+#pragma unroll 4
+    for (int dd = 0; dd < n; ++dd) {
+      const float4 xv = *reinterpret_cast<const float4*>(&sm.stage.x[dd][4 * tg]);
+#pragma unroll
+      for (int k = 0; k < kOut; ++k) {
+        const float wv = sm.stage.w[dd][og + 32 * k];  // columns >= P: unused sums
+        acc[0][k] = fmaf(xv.x, wv, acc[0][k]);
+        acc[1][k] = fmaf(xv.y, wv, acc[1][k]);
+        acc[2][k] = fmaf(xv.z, wv, acc[2][k]);
+        acc[3][k] = fmaf(xv.w, wv, acc[3][k]);
+      }
+    }
+  }
+  __syncthreads();  // the staging area becomes the partial tile
+#pragma unroll
+  for (int a = 0; a < 4; ++a)
+#pragma unroll
+    for (int k = 0; k < kOut; ++k) sm.part[4 * tg + a][og + 32 * k] = acc[a][k];
+  cluster.sync();  // every CTA's partial tile is complete and visible
+  // this CTA completes token rows [4 crank, 4 crank + 4): the 8 partials
+  // added in rank order
+  constexpr int kRows = kXpTokens / kXpCluster;
+  const float* parts[kXpCluster];  // every CTA's partial tile, mapped once
+#pragma unroll
+  for (int r = 0; r < kXpCluster; ++r) parts[r] = cluster.map_shared_rank(&sm.part[0][0], r);
+  for (int i = tid; i < kRows * P; i += kXpThreads) {
+    const int tt = crank * kRows + i / P, j = i % P;
+    float sum = 0.f;
+#pragma unroll
+    for (int r = 0; r < kXpCluster; ++r) sum += parts[r][tt * kXpRow + j];
+    const int t = t0 + tt;
+    if (t < seqlen) {
+      const int64_t row = (int64_t)b * seqlen + t;
+      if (j < rank)
+        dt[row * rank + j] = sum;
+      else if (j < rank + dstate)
+        Bm[row * dstate + (j - rank)] = sum;
+      else
+        Cm[row * dstate + (j - rank - dstate)] = sum;
+    }
+  }
+  cluster.sync();  // no CTA leaves while another still reads its shared memory
+}
+
+template <int kOut>
+cudaError_t launch_xproj(dim3 grid, cudaStream_t st, const float* x, const float* w, float* dt,
+                         float* Bm, float* Cm, int dim, int seqlen, int rank, int dstate) {
+  static std::once_flag once;
+  static cudaError_t attr = cudaSuccess;
+  std::call_once(once, [] {
+    attr = cudaFuncSetAttribute(xproj_kernel<kOut>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)kXpSmemBytes);
+  });
+  if (attr != cudaSuccess) return attr;
+  xproj_kernel<kOut><<<grid, kXpThreads, kXpSmemBytes, st>>>(x, w, dt, Bm, Cm, dim, seqlen, rank,
+                                                              dstate);
+  return cudaGetLastError();
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+bool overlap(const void* a, size_t abytes, const void* b, size_t bbytes) {
+  const auto a0 = reinterpret_cast<uintptr_t>(a), b0 = reinterpret_cast<uintptr_t>(b);
+  return a0 < b0 + bbytes && b0 < a0 + abytes;
+}
 
 }  // namespace
 
@@ -189,6 +325,44 @@ int mamba_causal_conv1d_silu(const float* x, int64_t x_batch_stride, const float
                                                            dim, seqlen, blocks_per_row, n_items,
                                                            (int)width);
   const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_last_error(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
+  return MAMBA_SCAN_OK;
+}
+
+int mamba_x_proj(const float* x, const float* weight, float* dt, float* B, float* C,
+                 int64_t batch, int64_t dim, int64_t seqlen, int64_t rank, int64_t dstate,
+                 void* stream) {
+  using mamba_scan::set_last_error;
+  if (batch < 0 || dim < 0 || seqlen < 0 || rank < 1 || dstate < 1 ||
+      rank + 2 * dstate > kXpMaxOut)
+    return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT,
+                          "x_proj: bad shape (rank + 2 * dstate must be 3.." +
+                              std::to_string(kXpMaxOut) + ")");
+  if (batch == 0 || seqlen == 0) return MAMBA_SCAN_OK;
+  if (!x || !weight || !dt || !B || !C || dim == 0)
+    return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "x_proj: NULL pointer or dim 0");
+  if (batch > 65535 || dim > ((int64_t)1 << 30) || seqlen > ((int64_t)1 << 30) ||
+      (seqlen + kXpTokens - 1) / kXpTokens * kXpCluster > 0x7FFFFFFF)
+    return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "x_proj: too large");
+  const size_t xb = (size_t)(batch * dim * seqlen) * 4, wb = (size_t)((rank + 2 * dstate) * dim) * 4;
+  const size_t dtb = (size_t)(batch * seqlen * rank) * 4, bcb = (size_t)(batch * seqlen * dstate) * 4;
+  const void* outs[3] = {dt, B, C};
+  const size_t out_bytes[3] = {dtb, bcb, bcb};
+  for (int i = 0; i < 3; ++i) {
+    if (overlap(outs[i], out_bytes[i], x, xb) || overlap(outs[i], out_bytes[i], weight, wb))
+      return set_last_error(MAMBA_SCAN_ERR_ALIASING, "x_proj: an output overlaps an input");
+    for (int k = i + 1; k < 3; ++k)
+      if (overlap(outs[i], out_bytes[i], outs[k], out_bytes[k]))
+        return set_last_error(MAMBA_SCAN_ERR_ALIASING, "x_proj: outputs overlap");
+  }
+  const dim3 grid((unsigned)((seqlen + kXpTokens - 1) / kXpTokens * kXpCluster), (unsigned)batch);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const cudaError_t e =
+      (rank + 2 * dstate <= 32 * 3)
+          ? launch_xproj<3>(grid, st, x, weight, dt, B, C, (int)dim, (int)seqlen, (int)rank,
+                            (int)dstate)
+          : launch_xproj<4>(grid, st, x, weight, dt, B, C, (int)dim, (int)seqlen, (int)rank,
+                            (int)dstate);
   if (e != cudaSuccess) return set_last_error(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
   return MAMBA_SCAN_OK;
 }

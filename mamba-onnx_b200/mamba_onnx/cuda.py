@@ -80,6 +80,8 @@ def library() -> ctypes.CDLL:
         lib.mamba_causal_conv1d_silu.restype = ctypes.c_int
         lib.mamba_causal_conv1d_silu.argtypes = [ctypes.c_void_p, ctypes.c_int64] + \
             [ctypes.c_void_p] * 3 + [ctypes.c_int64] * 4 + [ctypes.c_void_p]
+        lib.mamba_x_proj.restype = ctypes.c_int
+        lib.mamba_x_proj.argtypes = [ctypes.c_void_p] * 5 + [ctypes.c_int64] * 5 + [ctypes.c_void_p]
         lib.mamba_split_tf32.restype = ctypes.c_int
         lib.mamba_split_tf32.argtypes = [ctypes.c_void_p] + [ctypes.c_int64] * 3 + \
             [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p]
@@ -253,6 +255,29 @@ def causal_conv1d_silu(x, weight, bias=None, out=None, stream=None):
     if rc != STATUS_OK:
         _raise(rc, "causal_conv1d_silu")
     return out
+
+
+def x_proj(x, weight, rank: int, dstate: int, stream=None):
+    """Mamba's x_proj split into the scan's inputs: x [B, D, L] (contiguous
+    CUDA float32), weight [rank + 2*dstate, D]. Returns (dt [B, L, rank],
+    B [B, L, dstate], C [B, L, dstate]), all contiguous."""
+    import torch
+
+    if x.dim() != 3:
+        raise ValueError("x must be [batch, dim, seqlen]")
+    batch, dim, seqlen = x.shape
+    _check("x", x, (batch, dim, seqlen))
+    _check("weight", weight, (rank + 2 * dstate, dim))
+    kw = dict(dtype=torch.float32, device=x.device)
+    dt = torch.empty(batch, seqlen, rank, **kw)
+    Bm = torch.empty(batch, seqlen, dstate, **kw)
+    Cm = torch.empty(batch, seqlen, dstate, **kw)
+    st = stream if stream is not None else torch.cuda.current_stream(x.device)
+    rc = library().mamba_x_proj(_ptr(x), _ptr(weight), _ptr(dt), _ptr(Bm), _ptr(Cm), batch, dim,
+                                seqlen, rank, dstate, st.cuda_stream)
+    if rc != STATUS_OK:
+        _raise(rc, "x_proj")
+    return dt, Bm, Cm
 
 
 class SplitTF32:

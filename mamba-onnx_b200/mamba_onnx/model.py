@@ -15,8 +15,11 @@ Everything is float32. On CUDA the large projections (in_proj, out_proj and
 the LM head) over 16 or more tokens run on this package's tensor-core GEMM in
 3xTF32 form (operands split into two tf32 parts, three products summed with
 fp32 accumulation: fp32-accurate; ``GEMM = "cublas"`` selects torch's fp32
-GEMMs instead); x_proj and dt_proj (too few output tiles to fill the GPU)
-and single-token steps use torch's fp32 GEMMs. ``forward`` runs a whole sequence; ``step`` decodes one
+GEMMs instead); single-token steps use torch's fp32 GEMMs for those
+projections. x_proj over 16 or more tokens, whose 80-wide output is too
+narrow to fill the GPU with GEMM tiles, runs on this package's fp32 kernel
+(d_inner split over a cluster of 8 CTAs; dt, B and C written apart); dt_proj
+stays on torch's fp32 GEMM, which measured faster than a kernel of ours. ``forward`` runs a whole sequence; ``step`` decodes one
 token from a ``DecodeState`` (the convolution window and the 16 scan states
 per channel), which the scan carries in through ``h0`` and out through
 ``h_last``. On CUDA tensors the RMSNorms and the causal convolution + SiLU run
@@ -152,6 +155,9 @@ class MambaLayer(torch.nn.Module):
     def _ssm_inputs(self, x):
         """x [B, D, L] after conv + SiLU -> delta [B, D, L] (before bias), B, C [B, L, N]."""
         N, R = self.cfg.d_state, self.cfg.rank
+        if x.is_cuda and x.shape[2] >= TC_MIN_TOKENS:  # dt, B, C written apart, no copies
+            dt, Bm, Cm = cuda.x_proj(x.contiguous(), self.x_proj_weight.detach(), R, N)
+            return torch.matmul(self.dt_proj_weight, dt.transpose(1, 2)), Bm, Cm  # [B, D, L]
         if x.shape[0] == 1:  # 2-D GEMMs take the transposed views without copies
             x_dbl = torch.mm(x[0].t(), self.x_proj_weight.t()).unsqueeze(0)  # [1, L, R + 2N]
             delta = torch.mm(self.dt_proj_weight, x_dbl[0, :, :R].t()).unsqueeze(0)

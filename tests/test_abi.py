@@ -140,6 +140,17 @@ def test_gemm_and_split_validate_before_launch():
     assert gemm(ldc_m=0) == 1
 
 
+def test_x_proj_validates_before_launch():
+    lib = cuda.library()
+    f = 0x100000
+    # x_proj: rank + 2 dstate <= 128, outputs disjoint from inputs and each other
+    assert lib.mamba_x_proj(f, 2 * f, 3 * f, 4 * f, 5 * f, 1, 64, 16, 100, 16, None) == 1
+    assert lib.mamba_x_proj(f, 2 * f, 3 * f, 4 * f, 5 * f, 1, 64, 16, 0, 16, None) == 1
+    assert lib.mamba_x_proj(f, 2 * f, f + 64, 4 * f, 5 * f, 1, 64, 16, 8, 16, None) == 4
+    assert lib.mamba_x_proj(f, 2 * f, 3 * f, 3 * f + 64, 5 * f, 1, 64, 16, 8, 16, None) == 4
+    assert lib.mamba_x_proj(f, 2 * f, 3 * f, 4 * f, 5 * f, 0, 64, 16, 8, 16, None) == 0
+
+
 def test_empty_batch_is_a_no_op():
     lib = cuda.library()
     assert lib.mamba_scan_launch(0, ctypes.byref(_args(batch=0)), None, 0, None) == 0
