@@ -11,15 +11,15 @@
 // rounding of the lo parts), the same order as the fp32 rounding of the
 // accumulation itself.
 //
-// One CTA = one 128 x BN output tile (BN = 128 or 192), 10 or 14 warps:
+// One CTA = one 128 x BN output tile (BN = 64, 128 or 192), 6, 10 or 14 warps:
 // * the producer warp's lane 0 streams 32-wide K blocks of A_hi, A_lo,
-//   B_hi, B_lo by TMA (128-byte swizzle, 3 or 2 stages);
+//   B_hi, B_lo by TMA (128-byte swizzle, 4, 3 or 2 stages);
 // * the MMA warp's lane 0 waits for a stage, issues 4 K-steps x 3
 //   products of tcgen05.mma.kind::tf32 (M = 128, N = BN, K = 8) into a
 //   TMEM accumulator that starts from zero for every K block (corrections
 //   first, then hi*hi), and commits the stage back to the producer and the
 //   accumulator to the accumulator warps (two accumulators alternate);
-// * 8 or 12 accumulator warps (warp w owns TMEM lanes 32(w%4)..+31 = tile
+// * 4, 8 or 12 accumulator warps (warp w owns TMEM lanes 32(w%4)..+31 = tile
 //   rows, and 64 columns) read each K block's sums (tcgen05.ld), add them to
 //   fp32 registers, then store C with arbitrary strides, optionally adding
 //   a second matrix C_in (which may be C itself).
@@ -43,10 +43,15 @@ using mamba_scan::smem_u32;
 
 constexpr int BM = 128, BK = 32;  // BK fp32 = 128 bytes: one swizzled row
 
-// Tile configurations: 128 x 128 with a 3-stage ring (64 KB per stage), or
-// 128 x 192 with 2 stages (80 KB per stage) for outputs whose 128-wide tiles
-// would leave a small last wave (the in_proj shape: 192 tiles on 148 SMs,
-// against 144 tiles of 192 columns).
+// Tile configurations: 128 x 64 with a 4-stage ring (48 KB per stage),
+// 128 x 128 with 3 stages (64 KB), 128 x 192 with 2 stages (80 KB). The host
+// picks the width with the fewest waves x (128 + BN), the operand bytes a
+// CTA streams per K block being (2 * 128 + 2 * BN) x 32 x 4: in_proj (192
+// tiles of 128 on 148 SMs) takes 144 tiles of 192 (55.8 -> 43.8 us),
+// out_proj (48 tiles of 128) 96 tiles of 64 (37.4 -> 35.5 us); the LM head
+// measured the same at 192 and 128 (649 and 637-660 us). A K block costs a
+// CTA 0.7-1.2 us whatever the width: TMA delivery per SM, not the bytes of
+// the whole GPU, sets it.
 //
 // Warps 0..kAccWarps-1 accumulate and store: warp w owns TMEM lanes
 // 32(w%4)..+31 (tile rows) and columns [64(w/4), 64(w/4) + 64), so two or
@@ -71,7 +76,7 @@ struct Cfg {
   static constexpr int kThreads = 32 * (kAccWarps + 2);
   static constexpr uint32_t kATile = BM * BK * 4, kBTile = BN * BK * 4;
   static constexpr uint32_t kStageBytes = 2 * kATile + 2 * kBTile;
-  static constexpr int kTmemCols = (2 * BN <= 256) ? 256 : 512;  // a power of two >= 2 BN
+  static constexpr int kTmemCols = (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
   struct __align__(1024) Smem {
     float a_hi[kStages][BM * BK];
     float a_lo[kStages][BM * BK];
@@ -86,6 +91,7 @@ struct Cfg {
   static constexpr size_t kSmemBytes = sizeof(Smem) + 1024;  // + room to align the base
   static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
 };
+using Cfg64 = Cfg<64, 4>;
 using Cfg128 = Cfg<128, 3>;
 using Cfg192 = Cfg<192, 2>;
 
@@ -455,15 +461,18 @@ int device_sms() {
   return v;
 }
 
-// 192-column tiles when they take fewer waves x columns than 128-column ones
-// (one CTA per SM; a CTA's time grows with its tile's columns).
-bool use_wide_tiles(int64_t M, int64_t N, int sms) {
+// Tile width with the fewest waves x (128 + BN) (one CTA per SM; a CTA
+// streams (2 * 128 + 2 * BN) x 32 x 4 bytes per K block); ties go wider.
+int tile_width(int64_t M, int64_t N, int sms) {
   const int64_t m_tiles = (M + mamba_gemm::BM - 1) / mamba_gemm::BM;
   auto cost = [&](int64_t bn) {
     const int64_t tiles = m_tiles * ((N + bn - 1) / bn);
-    return (tiles + sms - 1) / sms * bn;
+    return (tiles + sms - 1) / sms * (mamba_gemm::BM + bn);
   };
-  return cost(192) < cost(128);
+  int best = 192;
+  for (int bn : {128, 64})
+    if (cost(bn) < cost(best)) best = bn;
+  return best;
 }
 
 template <class C>
@@ -561,10 +570,9 @@ int mamba_gemm_tf32x3(const float* a_hi, const float* a_lo, int64_t lda, const f
     return set_last_error(MAMBA_SCAN_ERR_ALIASING,
                           "gemm_tf32x3: c_in must be C itself or not overlap it");
   const int64_t m_tiles = (M + mamba_gemm::BM - 1) / mamba_gemm::BM;
-  if (m_tiles > 0x7FFFFFFF || (N + 127) / 128 > 65535)
+  if (m_tiles > 0x7FFFFFFF || (N + 63) / 64 > 65535)
     return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "gemm_tf32x3: too many tiles");
-  const bool wide = use_wide_tiles(M, N, device_sms());
-  const int bn = wide ? mamba_gemm::Cfg192::BN : mamba_gemm::Cfg128::BN;
+  const int bn = tile_width(M, N, device_sms());
   auto enc = gemm_encode_fn();
   mamba_gemm::GemmMaps maps;
   std::memset(&maps, 0, sizeof maps);
@@ -575,8 +583,9 @@ int mamba_gemm_tf32x3(const float* a_hi, const float* a_lo, int64_t lda, const f
     return set_last_error(MAMBA_SCAN_ERR_CUDA, "gemm_tf32x3: tensor map encoding failed");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   mamba_gemm::GemmParams p{c, c_in, ldc_m, ldc_n, (int)M, (int)N, (int)K};
-  const cudaError_t e = wide ? launch_gemm<mamba_gemm::Cfg192>(maps, p, m_tiles, st)
-                             : launch_gemm<mamba_gemm::Cfg128>(maps, p, m_tiles, st);
+  const cudaError_t e = bn == 192   ? launch_gemm<mamba_gemm::Cfg192>(maps, p, m_tiles, st)
+                        : bn == 128 ? launch_gemm<mamba_gemm::Cfg128>(maps, p, m_tiles, st)
+                                    : launch_gemm<mamba_gemm::Cfg64>(maps, p, m_tiles, st);
   if (e != cudaSuccess) return set_last_error(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
   return MAMBA_SCAN_OK;
 }
