@@ -157,6 +157,8 @@ class MambaLayer(torch.nn.Module):
         N, R = self.cfg.d_state, self.cfg.rank
         if x.is_cuda and x.shape[2] >= TC_MIN_TOKENS:  # dt, B, C written apart, no copies
             dt, Bm, Cm = cuda.x_proj(x.contiguous(), self.x_proj_weight.detach(), R, N)
+            if x.shape[0] == 1:  # a 2-D GEMM on the transposed view writes [D, L] directly
+                return torch.mm(self.dt_proj_weight, dt[0].t()).unsqueeze(0), Bm, Cm
             return torch.matmul(self.dt_proj_weight, dt.transpose(1, 2)), Bm, Cm  # [B, D, L]
         if x.shape[0] == 1:  # 2-D GEMMs take the transposed views without copies
             x_dbl = torch.mm(x[0].t(), self.x_proj_weight.t()).unsqueeze(0)  # [1, L, R + 2N]
