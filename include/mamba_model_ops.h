@@ -48,6 +48,20 @@ MAMBA_SCAN_API int mamba_causal_conv1d_silu(const float* x, int64_t x_batch_stri
                                             int64_t width, void* stream);
 
 /*
+ * One decoding step of the causal depthwise convolution + SiLU:
+ *   state[b, d, :] <- (state[b, d, 1:], x[b, d])   (oldest first)
+ *   y[b, d] = silu(bias[d] + sum_k weight[d, k] * state[b, d, k])
+ * state [batch][dim][width] is updated in place; x holds the new inputs,
+ * dim floats per batch entry `x_batch_stride` floats apart (the x half of a
+ * one-token in_proj output [batch][2*dim][1]); weight [dim][width], bias
+ * [dim] or NULL, y [batch][dim]. No two of state, x, y may overlap. width: 1..8.
+ */
+MAMBA_SCAN_API int mamba_causal_conv1d_step(float* state, const float* x, int64_t x_batch_stride,
+                                            const float* weight, const float* bias, float* y,
+                                            int64_t batch, int64_t dim, int64_t width,
+                                            void* stream);
+
+/*
  * Mamba's x_proj for every token, split into the scan's inputs:
  *   [dt | B | C][b, t, :] = weight . x[b, :, t]
  * x is [batch][dim][seqlen] contiguous (the convolution output, channel

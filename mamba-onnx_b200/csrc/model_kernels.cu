@@ -134,6 +134,32 @@ __global__ void __launch_bounds__(kConvThreads)
   }
 }
 
+// ------------------------------------------------------ convolution step
+
+// One decoding step of the causal convolution, one thread per (b, d): the
+// window state[b, d, :] (oldest first) shifts by one and takes the new input,
+// y[b, d] = silu(bias[d] + sum_k w[d, k] * state[b, d, k]).
+__global__ void __launch_bounds__(kConvThreads)
+    conv_step_kernel(float* __restrict__ state, const float* __restrict__ x, int64_t x_bstride,
+                     const float* __restrict__ w, const float* __restrict__ bias,
+                     float* __restrict__ y, int64_t batch, int64_t dim, int width) {
+  const int64_t i = (int64_t)blockIdx.x * kConvThreads + threadIdx.x;
+  if (i >= batch * dim) return;
+  const int64_t b = i / dim, d = i - b * dim;
+  float* st = state + i * width;
+  float acc = bias ? __ldg(bias + d) : 0.f;
+  float prev = __ldg(x + b * x_bstride + d);  // the newest input goes last
+#pragma unroll
+  for (int k = kConvMaxWidth - 1; k >= 0; --k) {
+    if (k >= width) continue;
+    const float cur = st[k];
+    st[k] = prev;
+    acc = fmaf(__ldg(w + d * width + k), prev, acc);
+    prev = cur;
+  }
+  y[i] = silu_exact(acc);
+}
+
 // ------------------------------------------------------------------ x_proj
 
 constexpr int kXpCluster = 8;    // CTAs per token block, each 1/8 of d_inner
@@ -363,6 +389,32 @@ int mamba_x_proj(const float* x, const float* weight, float* dt, float* B, float
                             (int)dstate)
           : launch_xproj<4>(grid, st, x, weight, dt, B, C, (int)dim, (int)seqlen, (int)rank,
                             (int)dstate);
+  if (e != cudaSuccess) return set_last_error(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
+  return MAMBA_SCAN_OK;
+}
+
+int mamba_causal_conv1d_step(float* state, const float* x, int64_t x_batch_stride,
+                             const float* weight, const float* bias, float* y, int64_t batch,
+                             int64_t dim, int64_t width, void* stream) {
+  using mamba_scan::set_last_error;
+  if (batch < 0 || dim < 0 || width < 1 || width > kConvMaxWidth)
+    return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT,
+                          "causal_conv1d_step: bad shape (width must be 1.." +
+                              std::to_string(kConvMaxWidth) + ")");
+  if (batch == 0 || dim == 0) return MAMBA_SCAN_OK;
+  if (!state || !x || !weight || !y)
+    return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "causal_conv1d_step: NULL pointer");
+  if (x_batch_stride < dim || batch * dim / kConvThreads >= ((int64_t)1 << 31))
+    return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT,
+                          "causal_conv1d_step: bad batch stride or too large");
+  const size_t sb = (size_t)(batch * dim * width) * 4, yb = (size_t)(batch * dim) * 4;
+  const size_t xb = (size_t)((batch - 1) * x_batch_stride + dim) * 4;
+  if (overlap(y, yb, state, sb) || overlap(y, yb, x, xb) || overlap(state, sb, x, xb))
+    return set_last_error(MAMBA_SCAN_ERR_ALIASING, "causal_conv1d_step: buffers overlap");
+  const unsigned grid = (unsigned)((batch * dim + kConvThreads - 1) / kConvThreads);
+  conv_step_kernel<<<grid, kConvThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      state, x, x_batch_stride, weight, bias, y, batch, dim, (int)width);
+  const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_last_error(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
   return MAMBA_SCAN_OK;
 }

@@ -80,6 +80,9 @@ def library() -> ctypes.CDLL:
         lib.mamba_causal_conv1d_silu.restype = ctypes.c_int
         lib.mamba_causal_conv1d_silu.argtypes = [ctypes.c_void_p, ctypes.c_int64] + \
             [ctypes.c_void_p] * 3 + [ctypes.c_int64] * 4 + [ctypes.c_void_p]
+        lib.mamba_causal_conv1d_step.restype = ctypes.c_int
+        lib.mamba_causal_conv1d_step.argtypes = [ctypes.c_void_p] * 2 + [ctypes.c_int64] + \
+            [ctypes.c_void_p] * 3 + [ctypes.c_int64] * 3 + [ctypes.c_void_p]
         lib.mamba_x_proj.restype = ctypes.c_int
         lib.mamba_x_proj.argtypes = [ctypes.c_void_p] * 5 + [ctypes.c_int64] * 5 + [ctypes.c_void_p]
         lib.mamba_split_tf32.restype = ctypes.c_int
@@ -255,6 +258,30 @@ def causal_conv1d_silu(x, weight, bias=None, out=None, stream=None):
     if rc != STATUS_OK:
         _raise(rc, "causal_conv1d_silu")
     return out
+
+
+def causal_conv1d_step(state, x, weight, bias=None, stream=None):
+    """One decoding step of silu(causal depthwise conv1d): state [B, D, K]
+    (contiguous, oldest input first) shifts in x [B, D] (rows contiguous, any
+    batch stride) in place; returns y [B, D]."""
+    import torch
+
+    batch, dim, width = state.shape
+    _check("state", state, (batch, dim, width))
+    if x.dim() != 2 or tuple(x.shape) != (batch, dim) or not x.is_cuda or \
+            x.dtype != torch.float32 or (dim > 1 and x.stride(1) != 1):
+        raise ValueError("x must be a [batch, dim] CUDA float32 tensor with contiguous rows")
+    w = weight.reshape(dim, -1)
+    _check("weight", w, (dim, width))
+    _check("bias", bias, (dim,))
+    y = torch.empty(batch, dim, dtype=torch.float32, device=state.device)
+    st = stream if stream is not None else torch.cuda.current_stream(state.device)
+    bstride = x.stride(0) if batch > 1 else dim
+    rc = library().mamba_causal_conv1d_step(_ptr(state), _ptr(x), bstride, _ptr(w), _ptr(bias),
+                                            _ptr(y), batch, dim, width, st.cuda_stream)
+    if rc != STATUS_OK:
+        _raise(rc, "causal_conv1d_step")
+    return y
 
 
 def x_proj(x, weight, rank: int, dstate: int, stream=None):

@@ -205,9 +205,13 @@ class MambaLayer(torch.nn.Module):
         the convolution, oldest first) and ssm_state [B, D, N] are updated."""
         D = self.cfg.d_inner
         xz = self._in_proj(h)  # [B, 2D, 1]
-        conv_state.copy_(torch.cat([conv_state[..., 1:], xz[:, :D]], dim=-1))
-        x = torch.sum(conv_state * self.conv_weight[:, 0, :], dim=-1) + self.conv_bias
-        x = F.silu(x).unsqueeze(-1).contiguous()  # [B, D, 1]
+        if xz.is_cuda:  # window shift, convolution and SiLU in one kernel
+            x = cuda.causal_conv1d_step(conv_state, xz[:, :D, 0], self.conv_weight.detach(),
+                                        self.conv_bias.detach()).unsqueeze(-1)  # [B, D, 1]
+        else:
+            conv_state.copy_(torch.cat([conv_state[..., 1:], xz[:, :D]], dim=-1))
+            x = torch.sum(conv_state * self.conv_weight[:, 0, :], dim=-1) + self.conv_bias
+            x = F.silu(x).unsqueeze(-1).contiguous()  # [B, D, 1]
         z = xz[:, D:].contiguous()
         delta, Bm, Cm = self._ssm_inputs(x)
         new_state = torch.empty_like(ssm_state)

@@ -140,6 +140,15 @@ def test_gemm_and_split_validate_before_launch():
     assert gemm(ldc_m=0) == 1
 
 
+def test_conv1d_step_validates_before_launch():
+    lib = cuda.library()
+    f = 0x100000
+    assert lib.mamba_causal_conv1d_step(f, 2 * f, 64, 3 * f, None, 4 * f, 1, 64, 9, None) == 1
+    assert lib.mamba_causal_conv1d_step(f, 2 * f, 63, 3 * f, None, 4 * f, 2, 64, 4, None) == 1
+    assert lib.mamba_causal_conv1d_step(f, 2 * f, 64, 3 * f, None, f + 16, 1, 64, 4, None) == 4
+    assert lib.mamba_causal_conv1d_step(f, 2 * f, 64, 3 * f, None, 4 * f, 0, 64, 4, None) == 0
+
+
 def test_x_proj_validates_before_launch():
     lib = cuda.library()
     f = 0x100000

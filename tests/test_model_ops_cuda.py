@@ -110,3 +110,22 @@ def test_x_proj_matches_float64(batch, dim, seqlen, rank, dstate):
     dt2, B2, C2 = cuda.x_proj(x, wx, rank, dstate)
     assert torch.equal(dt, dt2) and torch.equal(Bm, B2) and torch.equal(Cm, C2)
     assert cuda.check_device_error() == 0
+
+
+@pytest.mark.parametrize("batch,dim,width", [(1, 1536, 4), (3, 70, 4), (2, 33, 1), (2, 40, 8)])
+def test_conv1d_step_matches_torch_over_several_steps(batch, dim, width):
+    """Decoding steps of the causal convolution: the window shifts in the new
+    input (read through a batch stride, as the x half of a one-token in_proj
+    output) and y = silu(bias + w . window), for 5 consecutive steps."""
+    g = torch.Generator(device="cpu").manual_seed(dim + width)
+    state = torch.randn(batch, dim, width, generator=g).cuda()
+    w = torch.randn(dim, 1, width, generator=g).cuda()
+    bias = torch.randn(dim, generator=g).cuda()
+    ref_state = state.clone()
+    for step in range(5):
+        xz = torch.randn(batch, 2 * dim, 1, generator=g).cuda()
+        y = cuda.causal_conv1d_step(state, xz[:, :dim, 0], w, bias)
+        ref_state = torch.cat([ref_state[..., 1:], xz[:, :dim]], dim=-1)
+        ref = F.silu((ref_state * w[:, 0, :]).sum(-1) + bias)
+        assert torch.equal(state, ref_state), step
+        torch.testing.assert_close(y, ref, rtol=1e-5, atol=1e-6)
