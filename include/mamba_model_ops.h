@@ -69,7 +69,9 @@ MAMBA_SCAN_API int mamba_causal_conv1d_step(float* state, const float* x, int64_
  * go to dt [batch][seqlen][rank], the next `dstate` to B and the last
  * `dstate` to C ([batch][seqlen][dstate] each, the scan op's B/C layout).
  * fp32 throughout, deterministic; rank + 2*dstate <= 128. No output may
- * overlap an input or another output.
+ * overlap an input or another output. Up to 16 tokens (batch * seqlen, as
+ * when decoding) take 4 warps per output; more, a cluster of 8 CTAs per 32
+ * tokens splitting dim.
  */
 MAMBA_SCAN_API int mamba_x_proj(const float* x, const float* weight, float* dt, float* B, float* C,
                                 int64_t batch, int64_t dim, int64_t seqlen, int64_t rank,

@@ -261,6 +261,57 @@ __global__ void __cluster_dims__(kXpCluster, 1, 1) __launch_bounds__(kXpThreads)
   cluster.sync();  // no CTA leaves while another still reads its shared memory
 }
 
+// x_proj for a few tokens (decoding): 4 warps per (token, output), each
+// summing a quarter of d_inner with 8 independent partial sums per lane
+// (loads in flight together), then a fixed shuffle tree and a fixed-order
+// sum of the 4 warps' results through shared memory (deterministic).
+constexpr int kXpFewTokens = 16;  // batch * seqlen up to this take this kernel
+__global__ void __launch_bounds__(256)
+    xproj_few_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                     float* __restrict__ dt, float* __restrict__ Bm, float* __restrict__ Cm,
+                     int dim, int seqlen, int rank, int dstate) {
+  __shared__ float part[2][4];
+  const int P = rank + 2 * dstate;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int jj = warp >> 2, q = warp & 3;  // 2 outputs per CTA, 4 warps each
+  const int j = blockIdx.x * 2 + jj;
+  const int tok = blockIdx.y, b = tok / seqlen, t = tok - b * seqlen;
+  const int per = (dim + 3) / 4, d_lo = min(dim, q * per), d_hi = min(dim, d_lo + per);
+  float acc = 0.f;
+  if (j < P) {
+    const float* xr = x + (int64_t)b * dim * seqlen + t;
+    const float* wr = w + (int64_t)j * dim;
+    float a[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) a[u] = 0.f;
+    for (int d0 = d_lo + lane; d0 < d_hi; d0 += 32 * 8) {
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int d = d0 + 32 * u;
+        if (d < d_hi) a[u] = fmaf(__ldg(wr + d), __ldg(xr + (int64_t)d * seqlen), a[u]);
+      }
+    }
+    acc = ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
+  }
+  acc = warp_sum(acc);
+  if (lane == 0) part[jj][q] = acc;
+  __syncthreads();
+  if (threadIdx.x < 2) {
+    const int jo = blockIdx.x * 2 + threadIdx.x;
+    if (jo < P) {
+      const float sum = (part[threadIdx.x][0] + part[threadIdx.x][1]) +
+                        (part[threadIdx.x][2] + part[threadIdx.x][3]);
+      const int64_t row = (int64_t)b * seqlen + t;
+      if (jo < rank)
+        dt[row * rank + jo] = sum;
+      else if (jo < rank + dstate)
+        Bm[row * dstate + (jo - rank)] = sum;
+      else
+        Cm[row * dstate + (jo - rank - dstate)] = sum;
+    }
+  }
+}
+
 template <int kOut>
 cudaError_t launch_xproj(dim3 grid, cudaStream_t st, const float* x, const float* w, float* dt,
                          float* Bm, float* Cm, int dim, int seqlen, int rank, int dstate) {
@@ -381,8 +432,16 @@ int mamba_x_proj(const float* x, const float* weight, float* dt, float* B, float
       if (overlap(outs[i], out_bytes[i], outs[k], out_bytes[k]))
         return set_last_error(MAMBA_SCAN_ERR_ALIASING, "x_proj: outputs overlap");
   }
-  const dim3 grid((unsigned)((seqlen + kXpTokens - 1) / kXpTokens * kXpCluster), (unsigned)batch);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (batch * seqlen <= kXpFewTokens) {
+    const dim3 few((unsigned)((rank + 2 * dstate + 1) / 2), (unsigned)(batch * seqlen));
+    xproj_few_kernel<<<few, 256, 0, st>>>(x, weight, dt, B, C, (int)dim, (int)seqlen, (int)rank,
+                                          (int)dstate);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return set_last_error(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
+    return MAMBA_SCAN_OK;
+  }
+  const dim3 grid((unsigned)((seqlen + kXpTokens - 1) / kXpTokens * kXpCluster), (unsigned)batch);
   const cudaError_t e =
       (rank + 2 * dstate <= 32 * 3)
           ? launch_xproj<3>(grid, st, x, weight, dt, B, C, (int)dim, (int)seqlen, (int)rank,

@@ -16,10 +16,11 @@ the LM head) over 16 or more tokens run on this package's tensor-core GEMM in
 3xTF32 form (operands split into two tf32 parts, three products summed with
 fp32 accumulation: fp32-accurate; ``GEMM = "cublas"`` selects torch's fp32
 GEMMs instead); single-token steps use torch's fp32 GEMMs for those
-projections. x_proj over 16 or more tokens, whose 80-wide output is too
-narrow to fill the GPU with GEMM tiles, runs on this package's fp32 kernel
-(d_inner split over a cluster of 8 CTAs; dt, B and C written apart); dt_proj
-stays on torch's fp32 GEMM, which measured faster than a kernel of ours. ``forward`` runs a whole sequence; ``step`` decodes one
+projections. x_proj, whose 80-wide output is too narrow to fill the GPU with
+GEMM tiles, runs on this package's fp32 kernel (d_inner split over a cluster
+of 8 CTAs, or one warp per output when decoding; dt, B and C written apart);
+dt_proj stays on torch's fp32 GEMM, which measured faster than a kernel of
+ours. ``forward`` runs a whole sequence; ``step`` decodes one
 token from a ``DecodeState`` (the convolution window and the 16 scan states
 per channel), which the scan carries in through ``h0`` and out through
 ``h_last``. On CUDA tensors the RMSNorms and the causal convolution + SiLU run
@@ -155,7 +156,7 @@ class MambaLayer(torch.nn.Module):
     def _ssm_inputs(self, x):
         """x [B, D, L] after conv + SiLU -> delta [B, D, L] (before bias), B, C [B, L, N]."""
         N, R = self.cfg.d_state, self.cfg.rank
-        if x.is_cuda and x.shape[2] >= TC_MIN_TOKENS:  # dt, B, C written apart, no copies
+        if x.is_cuda:  # this package's x_proj: dt, B, C written apart, no copies
             dt, Bm, Cm = cuda.x_proj(x.contiguous(), self.x_proj_weight.detach(), R, N)
             if x.shape[0] == 1:  # a 2-D GEMM on the transposed view writes [D, L] directly
                 return torch.mm(self.dt_proj_weight, dt[0].t()).unsqueeze(0), Bm, Cm

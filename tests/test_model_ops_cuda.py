@@ -87,7 +87,9 @@ XPROJ_CASES = [
     # batch, dim, seqlen, rank, dstate
     (1, 1536, 1024, 48, 16),   # Mamba-130m
     (2, 200, 77, 8, 16),       # ragged: dim not a multiple of 8 x 32, seqlen of 64
-    (1, 96, 1, 48, 16),        # one token (decoding)
+    (1, 96, 1, 48, 16),        # one token (decoding): one warp per output
+    (4, 1536, 1, 48, 16),      # 4 decoding streams
+    (2, 300, 8, 80, 16),       # 16 tokens, P = 112, warp-per-output path
     (3, 520, 130, 80, 16),     # rank + 2 dstate = 112: the 8-outputs-per-thread path
 ]
 
