@@ -62,6 +62,26 @@ MAMBA_SCAN_API int mamba_causal_conv1d_step(float* state, const float* x, int64_
                                             void* stream);
 
 /*
+ * One decoding step of a Mamba block's SSM, dt_proj included: for each
+ * channel (b, d), with u = u[b, d] (the convolution output) and z = z[b, d]
+ * (z_batch_stride floats between batch entries),
+ *   delta = softplus(dt_weight[d] . dt[b] + dt_bias[d])
+ *   state[b, d, n] = exp(delta A[d, n]) state[b, d, n] + delta u B[b, n]
+ *   y[b, d] = (sum_n C[b, n] state[b, d, n] + D[d] u) * silu(z)
+ * i.e. SelectiveScanFusedExact over one step with h0 = h_last = state
+ * (updated in place) and delta = dt_proj(dt) computed here. dt [batch][rank]
+ * (rank <= 256), B and C [batch][dstate], dt_weight [dim][rank], dt_bias
+ * [dim] or NULL, A [dim][dstate], D [dim], state [batch][dim][dstate], y
+ * [batch][dim]. dstate must be 16; y and state must not overlap the inputs.
+ */
+MAMBA_SCAN_API int mamba_ssm_decode_step(const float* u, const float* z, int64_t z_batch_stride,
+                                         const float* dt, const float* B, const float* C,
+                                         const float* dt_weight, const float* dt_bias,
+                                         const float* A, const float* D, float* state, float* y,
+                                         int64_t batch, int64_t dim, int64_t rank, int64_t dstate,
+                                         void* stream);
+
+/*
  * Mamba's x_proj for every token, split into the scan's inputs:
  *   [dt | B | C][b, t, :] = weight . x[b, :, t]
  * x is [batch][dim][seqlen] contiguous (the convolution output, channel

@@ -160,6 +160,58 @@ __global__ void __launch_bounds__(kConvThreads)
   y[i] = silu_exact(acc);
 }
 
+// ------------------------------------------------------- SSM decode step
+
+constexpr int kSsmThreads = 128;  // channels per CTA
+constexpr int kSsmMaxRank = 256;
+constexpr int kSsmN = 16;         // d_state (as the scan op)
+
+// One decoding step of a SelectiveScanFusedExact block for channel (b, d),
+// with dt_proj fused in front and the state updated in place:
+//   delta = softplus(W_dt[d] . dt[b] + bias[d])   (the op's branches: > 20 -> x,
+//                                                  < -20 -> e^x, else log1p(e^x))
+//   h[n]  = exp(delta A[d,n]) h[n] + delta u B[b,n]
+//   y     = (sum_n C[b,n] h[n] + D[d] u) * silu(z)
+// dt, B and C of the CTA's batch entry are staged in shared memory.
+__global__ void __launch_bounds__(kSsmThreads)
+    ssm_step_kernel(const float* __restrict__ u, const float* __restrict__ z, int64_t z_bstride,
+                    const float* __restrict__ dt, const float* __restrict__ Bm,
+                    const float* __restrict__ Cm, const float* __restrict__ w_dt,
+                    const float* __restrict__ dt_bias, const float* __restrict__ A,
+                    const float* __restrict__ Dskip, float* __restrict__ state,
+                    float* __restrict__ y, int dim, int rank) {
+  __shared__ float sdt[kSsmMaxRank];
+  __shared__ float sB[kSsmN], sC[kSsmN];
+  const int b = blockIdx.y;
+  for (int r = threadIdx.x; r < rank; r += kSsmThreads) sdt[r] = __ldg(dt + (int64_t)b * rank + r);
+  if (threadIdx.x < kSsmN) {
+    sB[threadIdx.x] = __ldg(Bm + b * kSsmN + threadIdx.x);
+    sC[threadIdx.x] = __ldg(Cm + b * kSsmN + threadIdx.x);
+  }
+  __syncthreads();
+  const int d = blockIdx.x * kSsmThreads + threadIdx.x;
+  if (d >= dim) return;
+  const float* wr = w_dt + (int64_t)d * rank;
+  float xd = dt_bias ? __ldg(dt_bias + d) : 0.f;
+  for (int r = 0; r < rank; ++r) xd = fmaf(__ldg(wr + r), sdt[r], xd);
+  const float e = expf(xd);
+  const float delta = xd > 20.f ? xd : (xd < -20.f ? e : log1pf(e));
+  const int64_t row = (int64_t)b * dim + d;
+  const float uv = __ldg(u + row);
+  const float du = delta * uv;
+  float* h = state + row * kSsmN;
+  const float* a = A + (int64_t)d * kSsmN;
+  float acc = 0.f;
+#pragma unroll
+  for (int n = 0; n < kSsmN; ++n) {
+    const float hn = fmaf(expf(delta * __ldg(a + n)), h[n], du * sB[n]);
+    h[n] = hn;
+    acc = fmaf(sC[n], hn, acc);
+  }
+  const float zv = __ldg(z + (int64_t)b * z_bstride + d);
+  y[row] = fmaf(__ldg(Dskip + d), uv, acc) * (zv / (1.f + expf(-zv)));
+}
+
 // ------------------------------------------------------------------ x_proj
 
 constexpr int kXpCluster = 8;    // CTAs per token block, each 1/8 of d_inner
@@ -473,6 +525,44 @@ int mamba_causal_conv1d_step(float* state, const float* x, int64_t x_batch_strid
   const unsigned grid = (unsigned)((batch * dim + kConvThreads - 1) / kConvThreads);
   conv_step_kernel<<<grid, kConvThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       state, x, x_batch_stride, weight, bias, y, batch, dim, (int)width);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_last_error(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
+  return MAMBA_SCAN_OK;
+}
+
+int mamba_ssm_decode_step(const float* u, const float* z, int64_t z_batch_stride,
+                          const float* dt, const float* B, const float* C, const float* dt_weight,
+                          const float* dt_bias, const float* A, const float* D, float* state,
+                          float* y, int64_t batch, int64_t dim, int64_t rank, int64_t dstate,
+                          void* stream) {
+  using mamba_scan::set_last_error;
+  if (dstate != kSsmN)
+    return set_last_error(MAMBA_SCAN_ERR_UNSUPPORTED_DSTATE,
+                          "ssm_decode_step: only dstate=16 is supported");
+  if (batch < 0 || dim < 0 || rank < 1 || rank > kSsmMaxRank)
+    return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT,
+                          "ssm_decode_step: bad shape (rank 1.." + std::to_string(kSsmMaxRank) + ")");
+  if (batch == 0 || dim == 0) return MAMBA_SCAN_OK;
+  if (!u || !z || !dt || !B || !C || !dt_weight || !A || !D || !state || !y)
+    return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "ssm_decode_step: NULL pointer");
+  if (z_batch_stride < dim || batch > 65535 || dim > ((int64_t)1 << 30))
+    return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT,
+                          "ssm_decode_step: bad z batch stride or too large");
+  const size_t yb = (size_t)(batch * dim) * 4, sb = yb * kSsmN;
+  const void* ins[] = {u, z, dt, B, C, dt_weight, A, D};
+  const size_t in_bytes[] = {yb, (size_t)((batch - 1) * z_batch_stride + dim) * 4,
+                             (size_t)(batch * rank) * 4, (size_t)(batch * kSsmN) * 4,
+                             (size_t)(batch * kSsmN) * 4, (size_t)(dim * rank) * 4,
+                             (size_t)(dim * kSsmN) * 4, (size_t)dim * 4};
+  for (int i = 0; i < 8; ++i)
+    if (overlap(y, yb, ins[i], in_bytes[i]) || overlap(state, sb, ins[i], in_bytes[i]))
+      return set_last_error(MAMBA_SCAN_ERR_ALIASING,
+                            "ssm_decode_step: y or state overlaps an input");
+  if (overlap(y, yb, state, sb))
+    return set_last_error(MAMBA_SCAN_ERR_ALIASING, "ssm_decode_step: y overlaps state");
+  const dim3 grid((unsigned)((dim + kSsmThreads - 1) / kSsmThreads), (unsigned)batch);
+  ssm_step_kernel<<<grid, kSsmThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      u, z, z_batch_stride, dt, B, C, dt_weight, dt_bias, A, D, state, y, (int)dim, (int)rank);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_last_error(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
   return MAMBA_SCAN_OK;

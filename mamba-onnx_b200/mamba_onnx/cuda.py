@@ -83,6 +83,9 @@ def library() -> ctypes.CDLL:
         lib.mamba_causal_conv1d_step.restype = ctypes.c_int
         lib.mamba_causal_conv1d_step.argtypes = [ctypes.c_void_p] * 2 + [ctypes.c_int64] + \
             [ctypes.c_void_p] * 3 + [ctypes.c_int64] * 3 + [ctypes.c_void_p]
+        lib.mamba_ssm_decode_step.restype = ctypes.c_int
+        lib.mamba_ssm_decode_step.argtypes = [ctypes.c_void_p] * 2 + [ctypes.c_int64] + \
+            [ctypes.c_void_p] * 9 + [ctypes.c_int64] * 4 + [ctypes.c_void_p]
         lib.mamba_x_proj.restype = ctypes.c_int
         lib.mamba_x_proj.argtypes = [ctypes.c_void_p] * 5 + [ctypes.c_int64] * 5 + [ctypes.c_void_p]
         lib.mamba_split_tf32.restype = ctypes.c_int
@@ -281,6 +284,37 @@ def causal_conv1d_step(state, x, weight, bias=None, stream=None):
                                             _ptr(y), batch, dim, width, st.cuda_stream)
     if rc != STATUS_OK:
         _raise(rc, "causal_conv1d_step")
+    return y
+
+
+def ssm_decode_step(u, z, dt, B, C, dt_weight, dt_bias, A, D, state, stream=None):
+    """One decoding step of a SelectiveScanFusedExact block with dt_proj fused
+    in front: u [batch, dim], z [batch, dim] (rows contiguous, any batch
+    stride), dt [batch, rank], B/C [batch, 16], dt_weight [dim, rank],
+    dt_bias [dim] or None, A [dim, 16], D [dim]; state [batch, dim, 16] is
+    updated in place. Returns y [batch, dim]."""
+    import torch
+
+    batch, dim = u.shape
+    rank, dstate = dt.shape[1], A.shape[1]
+    for name, t, shape in [("u", u, (batch, dim)), ("dt", dt, (batch, rank)),
+                           ("B", B, (batch, dstate)), ("C", C, (batch, dstate)),
+                           ("dt_weight", dt_weight, (dim, rank)), ("dt_bias", dt_bias, (dim,)),
+                           ("A", A, (dim, dstate)), ("D", D, (dim,)),
+                           ("state", state, (batch, dim, dstate))]:
+        _check(name, t, shape)
+    if tuple(z.shape) != (batch, dim) or not z.is_cuda or z.dtype != torch.float32 or \
+            (dim > 1 and z.stride(1) != 1):
+        raise ValueError("z must be a [batch, dim] CUDA float32 tensor with contiguous rows")
+    y = torch.empty(batch, dim, dtype=torch.float32, device=u.device)
+    st = stream if stream is not None else torch.cuda.current_stream(u.device)
+    zstride = z.stride(0) if batch > 1 else dim
+    rc = library().mamba_ssm_decode_step(_ptr(u), _ptr(z), zstride, _ptr(dt), _ptr(B), _ptr(C),
+                                         _ptr(dt_weight), _ptr(dt_bias), _ptr(A), _ptr(D),
+                                         _ptr(state), _ptr(y), batch, dim, rank, dstate,
+                                         st.cuda_stream)
+    if rc != STATUS_OK:
+        _raise(rc, "ssm_decode_step")
     return y
 
 

@@ -204,15 +204,23 @@ class MambaLayer(torch.nn.Module):
     def step(self, h, A, conv_state, ssm_state):
         """One token: h [B, 1, d_model]; conv_state [B, D, d_conv] (last inputs of
         the convolution, oldest first) and ssm_state [B, D, N] are updated."""
-        D = self.cfg.d_inner
+        D, N, R = self.cfg.d_inner, self.cfg.d_state, self.cfg.rank
         xz = self._in_proj(h)  # [B, 2D, 1]
-        if xz.is_cuda:  # window shift, convolution and SiLU in one kernel
+        if xz.is_cuda:
+            # this package's kernels: the convolution step (window shift,
+            # conv, SiLU), x_proj, then dt_proj + the scan step + the state
+            # update in one kernel (SelectiveScanFusedExact at seqlen 1)
             x = cuda.causal_conv1d_step(conv_state, xz[:, :D, 0], self.conv_weight.detach(),
-                                        self.conv_bias.detach()).unsqueeze(-1)  # [B, D, 1]
-        else:
-            conv_state.copy_(torch.cat([conv_state[..., 1:], xz[:, :D]], dim=-1))
-            x = torch.sum(conv_state * self.conv_weight[:, 0, :], dim=-1) + self.conv_bias
-            x = F.silu(x).unsqueeze(-1).contiguous()  # [B, D, 1]
+                                        self.conv_bias.detach())  # [B, D]
+            dt, Bm, Cm = cuda.x_proj(x.unsqueeze(-1), self.x_proj_weight.detach(), R, N)
+            y = cuda.ssm_decode_step(x, xz[:, D:, 0], dt[:, 0], Bm[:, 0], Cm[:, 0],
+                                     self.dt_proj_weight.detach(), self.dt_proj_bias.detach(),
+                                     A, self.D.detach(), ssm_state)
+            return add_out_proj(h, y.unsqueeze(-1), self.out_proj_weight)
+        # the same step in torch operations around the scan op
+        conv_state.copy_(torch.cat([conv_state[..., 1:], xz[:, :D]], dim=-1))
+        x = torch.sum(conv_state * self.conv_weight[:, 0, :], dim=-1) + self.conv_bias
+        x = F.silu(x).unsqueeze(-1).contiguous()  # [B, D, 1]
         z = xz[:, D:].contiguous()
         delta, Bm, Cm = self._ssm_inputs(x)
         new_state = torch.empty_like(ssm_state)

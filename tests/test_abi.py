@@ -149,6 +149,21 @@ def test_conv1d_step_validates_before_launch():
     assert lib.mamba_causal_conv1d_step(f, 2 * f, 64, 3 * f, None, 4 * f, 0, 64, 4, None) == 0
 
 
+def test_ssm_decode_step_validates_before_launch():
+    lib = cuda.library()
+    f = 0x100000
+
+    def call(dstate=16, rank=8, state=10 * f, y=11 * f, zs=64, batch=1):
+        return lib.mamba_ssm_decode_step(f, 2 * f, zs, 3 * f, 4 * f, 5 * f, 6 * f, 7 * f, 8 * f,
+                                         9 * f, state, y, batch, 64, rank, dstate, None)
+
+    assert call(dstate=8) == 2
+    assert call(rank=0) == 1 and call(rank=300) == 1
+    assert call(zs=63, batch=2) == 1
+    assert call(y=f + 16) == 4 and call(state=8 * f) == 4
+    assert call(batch=0) == 0
+
+
 def test_x_proj_validates_before_launch():
     lib = cuda.library()
     f = 0x100000

@@ -131,3 +131,36 @@ def test_conv1d_step_matches_torch_over_several_steps(batch, dim, width):
         ref = F.silu((ref_state * w[:, 0, :]).sum(-1) + bias)
         assert torch.equal(state, ref_state), step
         torch.testing.assert_close(y, ref, rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("batch,dim,rank", [(1, 1536, 48), (3, 200, 8), (2, 130, 64)])
+def test_ssm_decode_step_matches_the_scan_op(batch, dim, rank):
+    """The fused decode step (dt_proj, softplus, exp(delta A) update in place,
+    C.h + D u, silu(z) gate) equals SelectiveScanFusedExact at seqlen 1 with
+    h0/h_last and dt_proj computed by torch, for 3 consecutive steps
+    (tolerance of the op's Exact tests: 1e-5 relative)."""
+    g = torch.Generator(device="cpu").manual_seed(dim + rank)
+    dev = torch.device("cuda", 0)
+    N = 16
+    rnd = lambda *s, sc=1.0: (torch.randn(*s, generator=g) * sc).to(dev)  # noqa: E731
+    wdt, bias = rnd(dim, rank, sc=0.1), rnd(dim, sc=0.5) - 2.0
+    A = -torch.arange(1, N + 1, dtype=torch.float32, device=dev).repeat(dim, 1) * \
+        (rnd(dim, 1).abs() + 0.5)
+    Dv = rnd(dim)
+    state = rnd(batch, dim, N, sc=0.3)
+    ref_state = state.clone()
+    for step in range(3):
+        u, dt = rnd(batch, dim), rnd(batch, rank)
+        zz = rnd(batch, 2 * dim)[:, dim:]  # strided z, as the z half of in_proj's output
+        Bm, Cm = rnd(batch, N), rnd(batch, N)
+        y = cuda.ssm_decode_step(u, zz, dt, Bm, Cm, wdt, bias, A, Dv, state)
+        delta = torch.matmul(dt, wdt.t()).unsqueeze(-1)  # [B, D, 1] before the bias
+        new = torch.empty_like(ref_state)
+        ref = cuda.selective_scan("SelectiveScanFusedExact", u.unsqueeze(-1).contiguous(), delta,
+                                  A, Bm.unsqueeze(1).contiguous(), Cm.unsqueeze(1).contiguous(),
+                                  Dv, zz.unsqueeze(-1).contiguous(), delta_bias=bias,
+                                  h0=ref_state, h_last=new)
+        ref_state = new
+        torch.testing.assert_close(y, ref[..., 0], rtol=1e-5, atol=1e-6)
+        torch.testing.assert_close(state, ref_state, rtol=1e-5, atol=1e-6)
+    assert cuda.check_device_error() == 0
