@@ -915,8 +915,8 @@ def run_decode(args):
                     "h2d_bytes_per_step": host_ids.numel() * 8,
                     "d2h_bytes_per_step": host_next.numel() * 8, "ms_per_step": e2e_ms,
                     "path": "pinned token ids -> graph replay -> argmax token to host"},
-            # this package's kernels per token: per block RMSNorm, the
-            # convolution step, x_proj and the fused dt_proj + scan step;
+            # this package's kernels per token: per block RMSNorm + in_proj,
+            # the convolution step, x_proj and the fused dt_proj + scan step;
             # then the final RMSNorm
             "gpu_launches": (model.cfg.n_layer * 4 + 1) * args.steps,
             "clocks": clocks.summary()}), flush=True)

@@ -62,6 +62,18 @@ MAMBA_SCAN_API int mamba_causal_conv1d_step(float* state, const float* x, int64_
                                             void* stream);
 
 /*
+ * RMSNorm followed by a matrix-vector product, for a few tokens (a block's
+ * norm and in_proj when decoding):
+ *   out[b, j] = sum_c weight[j, c] * x[b, c] * rsqrt(mean(x[b]^2) + eps) * norm_weight[c]
+ * x [batch][cols], norm_weight [cols], weight [rows_out][cols] (16-byte
+ * aligned), out [batch][rows_out], not overlapping the inputs; cols a
+ * multiple of 4, at most 4096.
+ */
+MAMBA_SCAN_API int mamba_rmsnorm_gemv(const float* x, const float* norm_weight, float eps,
+                                      const float* weight, float* out, int64_t batch,
+                                      int64_t cols, int64_t rows_out, void* stream);
+
+/*
  * One decoding step of a Mamba block's SSM, dt_proj included: for each
  * channel (b, d), with u = u[b, d] (the convolution output) and z = z[b, d]
  * (z_batch_stride floats between batch entries),

@@ -160,6 +160,54 @@ __global__ void __launch_bounds__(kConvThreads)
   y[i] = silu_exact(acc);
 }
 
+// ---------------------------------------------------- RMSNorm + GEMV step
+
+constexpr int kNgThreads = 256;  // 8 warps, one output row each per pass
+constexpr int kNgMaxCols = 4096;
+
+// out[b, j] = weight[j] . (x[b] * rsqrt(mean(x[b]^2) + eps) * norm_w), for
+// a few tokens (decoding): every CTA normalises its token's row into shared
+// memory (cols <= 4096), then each warp takes output rows j with float4
+// loads of weight[j] and a fixed shuffle tree (deterministic).
+__global__ void __launch_bounds__(kNgThreads)
+    norm_gemv_kernel(const float* __restrict__ x, const float* __restrict__ norm_w,
+                     const float* __restrict__ weight, float* __restrict__ out, int cols,
+                     int rows_out, float eps) {
+  __shared__ __align__(16) float xn[kNgMaxCols];
+  __shared__ float red[kNgThreads / 32];
+  const int b = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float* xr = x + (int64_t)b * cols;
+  float ss = 0.f;
+  for (int c = threadIdx.x; c < cols; c += kNgThreads) {
+    const float v = __ldg(xr + c);
+    xn[c] = v;
+    ss = fmaf(v, v, ss);
+  }
+  ss = warp_sum(ss);
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int w = 0; w < kNgThreads / 32; ++w) tot += red[w];
+  const float inv = rsqrtf(tot / (float)cols + eps);
+  for (int c = threadIdx.x; c < cols; c += kNgThreads) xn[c] = xn[c] * inv * __ldg(norm_w + c);
+  __syncthreads();
+  const int j = blockIdx.x * (kNgThreads / 32) + warp;
+  if (j >= rows_out) return;
+  const float* wr = weight + (int64_t)j * cols;
+  float acc = 0.f;
+  for (int c = lane * 4; c < cols; c += 128) {
+    const float4 wv = __ldg(reinterpret_cast<const float4*>(wr + c));
+    const float4 xv = *reinterpret_cast<const float4*>(&xn[c]);
+    acc = fmaf(wv.x, xv.x, acc);
+    acc = fmaf(wv.y, xv.y, acc);
+    acc = fmaf(wv.z, xv.z, acc);
+    acc = fmaf(wv.w, xv.w, acc);
+  }
+  acc = warp_sum(acc);
+  if (lane == 0) out[(int64_t)b * rows_out + j] = acc;
+}
+
 // ------------------------------------------------------- SSM decode step
 
 constexpr int kSsmThreads = 128;  // channels per CTA
@@ -563,6 +611,32 @@ int mamba_ssm_decode_step(const float* u, const float* z, int64_t z_batch_stride
   const dim3 grid((unsigned)((dim + kSsmThreads - 1) / kSsmThreads), (unsigned)batch);
   ssm_step_kernel<<<grid, kSsmThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       u, z, z_batch_stride, dt, B, C, dt_weight, dt_bias, A, D, state, y, (int)dim, (int)rank);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_last_error(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
+  return MAMBA_SCAN_OK;
+}
+
+int mamba_rmsnorm_gemv(const float* x, const float* norm_weight, float eps, const float* weight,
+                       float* out, int64_t batch, int64_t cols, int64_t rows_out, void* stream) {
+  using mamba_scan::set_last_error;
+  if (batch < 0 || cols < 1 || cols > kNgMaxCols || cols % 4 != 0 || rows_out < 0)
+    return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT,
+                          "rmsnorm_gemv: cols must be a multiple of 4 in 4.." +
+                              std::to_string(kNgMaxCols));
+  if (batch == 0 || rows_out == 0) return MAMBA_SCAN_OK;
+  if (!x || !norm_weight || !weight || !out)
+    return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "rmsnorm_gemv: NULL pointer");
+  if (!aligned16(weight) || batch > 65535 || rows_out > ((int64_t)1 << 30))
+    return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT,
+                          "rmsnorm_gemv: weight must be 16-byte aligned; or too large");
+  const size_t ob = (size_t)(batch * rows_out) * 4;
+  if (overlap(out, ob, x, (size_t)(batch * cols) * 4) ||
+      overlap(out, ob, weight, (size_t)(rows_out * cols) * 4) ||
+      overlap(out, ob, norm_weight, (size_t)cols * 4))
+    return set_last_error(MAMBA_SCAN_ERR_ALIASING, "rmsnorm_gemv: out overlaps an input");
+  const dim3 grid((unsigned)((rows_out + kNgThreads / 32 - 1) / (kNgThreads / 32)), (unsigned)batch);
+  norm_gemv_kernel<<<grid, kNgThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      x, norm_weight, weight, out, (int)cols, (int)rows_out, eps);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_last_error(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
   return MAMBA_SCAN_OK;

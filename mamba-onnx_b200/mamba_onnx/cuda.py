@@ -83,6 +83,9 @@ def library() -> ctypes.CDLL:
         lib.mamba_causal_conv1d_step.restype = ctypes.c_int
         lib.mamba_causal_conv1d_step.argtypes = [ctypes.c_void_p] * 2 + [ctypes.c_int64] + \
             [ctypes.c_void_p] * 3 + [ctypes.c_int64] * 3 + [ctypes.c_void_p]
+        lib.mamba_rmsnorm_gemv.restype = ctypes.c_int
+        lib.mamba_rmsnorm_gemv.argtypes = [ctypes.c_void_p] * 2 + [ctypes.c_float] + \
+            [ctypes.c_void_p] * 2 + [ctypes.c_int64] * 3 + [ctypes.c_void_p]
         lib.mamba_ssm_decode_step.restype = ctypes.c_int
         lib.mamba_ssm_decode_step.argtypes = [ctypes.c_void_p] * 2 + [ctypes.c_int64] + \
             [ctypes.c_void_p] * 9 + [ctypes.c_int64] * 4 + [ctypes.c_void_p]
@@ -285,6 +288,25 @@ def causal_conv1d_step(state, x, weight, bias=None, stream=None):
     if rc != STATUS_OK:
         _raise(rc, "causal_conv1d_step")
     return y
+
+
+def rmsnorm_gemv(x, norm_weight, eps: float, weight, stream=None):
+    """weight @ rmsnorm(x) for a few tokens: x [batch, cols], norm_weight
+    [cols], weight [rows_out, cols] -> [batch, rows_out]."""
+    import torch
+
+    batch, cols = x.shape
+    rows_out = weight.shape[0]
+    _check("x", x, (batch, cols))
+    _check("norm_weight", norm_weight, (cols,))
+    _check("weight", weight, (rows_out, cols))
+    out = torch.empty(batch, rows_out, dtype=torch.float32, device=x.device)
+    st = stream if stream is not None else torch.cuda.current_stream(x.device)
+    rc = library().mamba_rmsnorm_gemv(_ptr(x), _ptr(norm_weight), float(eps), _ptr(weight),
+                                      _ptr(out), batch, cols, rows_out, st.cuda_stream)
+    if rc != STATUS_OK:
+        _raise(rc, "rmsnorm_gemv")
+    return out
 
 
 def ssm_decode_step(u, z, dt, B, C, dt_weight, dt_bias, A, D, state, stream=None):

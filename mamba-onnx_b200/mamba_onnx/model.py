@@ -205,11 +205,13 @@ class MambaLayer(torch.nn.Module):
         """One token: h [B, 1, d_model]; conv_state [B, D, d_conv] (last inputs of
         the convolution, oldest first) and ssm_state [B, D, N] are updated."""
         D, N, R = self.cfg.d_inner, self.cfg.d_state, self.cfg.rank
-        xz = self._in_proj(h)  # [B, 2D, 1]
-        if xz.is_cuda:
-            # this package's kernels: the convolution step (window shift,
-            # conv, SiLU), x_proj, then dt_proj + the scan step + the state
-            # update in one kernel (SelectiveScanFusedExact at seqlen 1)
+        if h.is_cuda:
+            # this package's kernels: RMSNorm + in_proj, the convolution step
+            # (window shift, conv, SiLU), x_proj, then dt_proj + the scan step
+            # + the state update in one kernel (SelectiveScanFusedExact at
+            # seqlen 1)
+            xz = cuda.rmsnorm_gemv(h[:, 0], self.norm_weight.detach(), self.cfg.rms_eps,
+                                   self.in_proj_weight.detach()).unsqueeze(-1)  # [B, 2D, 1]
             x = cuda.causal_conv1d_step(conv_state, xz[:, :D, 0], self.conv_weight.detach(),
                                         self.conv_bias.detach())  # [B, D]
             dt, Bm, Cm = cuda.x_proj(x.unsqueeze(-1), self.x_proj_weight.detach(), R, N)
@@ -218,6 +220,7 @@ class MambaLayer(torch.nn.Module):
                                      A, self.D.detach(), ssm_state)
             return add_out_proj(h, y.unsqueeze(-1), self.out_proj_weight)
         # the same step in torch operations around the scan op
+        xz = self._in_proj(h)  # [B, 2D, 1]
         conv_state.copy_(torch.cat([conv_state[..., 1:], xz[:, :D]], dim=-1))
         x = torch.sum(conv_state * self.conv_weight[:, 0, :], dim=-1) + self.conv_bias
         x = F.silu(x).unsqueeze(-1).contiguous()  # [B, D, 1]

@@ -164,6 +164,16 @@ def test_ssm_decode_step_validates_before_launch():
     assert call(batch=0) == 0
 
 
+def test_rmsnorm_gemv_validates_before_launch():
+    lib = cuda.library()
+    f = 0x100000
+    assert lib.mamba_rmsnorm_gemv(f, 2 * f, 1e-5, 3 * f, 4 * f, 1, 66, 8, None) == 1  # cols % 4
+    assert lib.mamba_rmsnorm_gemv(f, 2 * f, 1e-5, 3 * f, 4 * f, 1, 8192, 8, None) == 1
+    assert lib.mamba_rmsnorm_gemv(f, 2 * f, 1e-5, 3 * f + 4, 4 * f, 1, 64, 8, None) == 1
+    assert lib.mamba_rmsnorm_gemv(f, 2 * f, 1e-5, 3 * f, f + 8, 1, 64, 8, None) == 4
+    assert lib.mamba_rmsnorm_gemv(f, 2 * f, 1e-5, 3 * f, 4 * f, 0, 64, 8, None) == 0
+
+
 def test_x_proj_validates_before_launch():
     lib = cuda.library()
     f = 0x100000

@@ -164,3 +164,18 @@ def test_ssm_decode_step_matches_the_scan_op(batch, dim, rank):
         torch.testing.assert_close(y, ref[..., 0], rtol=1e-5, atol=1e-6)
         torch.testing.assert_close(state, ref_state, rtol=1e-5, atol=1e-6)
     assert cuda.check_device_error() == 0
+
+
+@pytest.mark.parametrize("batch,cols,rows", [(1, 768, 3072), (3, 64, 10), (2, 1024, 777)])
+def test_rmsnorm_gemv_matches_float64(batch, cols, rows):
+    """weight @ rmsnorm(x) for decoding tokens against float64: normwise 1e-6."""
+    g = torch.Generator(device="cpu").manual_seed(cols + rows)
+    x = torch.randn(batch, cols, generator=g).cuda()
+    nw = (1 + 0.1 * torch.randn(cols, generator=g)).cuda()
+    w = (torch.randn(rows, cols, generator=g) * 0.02).cuda()
+    got = cuda.rmsnorm_gemv(x, nw, 1e-5, w)
+    x64 = x.double()
+    hn = x64 * torch.rsqrt(x64.pow(2).mean(-1, keepdim=True) + 1e-5) * nw.double()
+    ref = hn @ w.double().t()
+    assert float((got.double() - ref).norm() / ref.norm()) < 1e-6
+    assert torch.equal(got, cuda.rmsnorm_gemv(x, nw, 1e-5, w))
