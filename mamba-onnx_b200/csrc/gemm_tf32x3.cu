@@ -232,6 +232,10 @@ __global__ void __launch_bounds__(C::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
+  // launched as a programmatic dependent launch: the set-up above overlaps
+  // the previous kernel; the operands and C are touched only after it ends
+  mamba_scan::pdl_trigger();
+  mamba_scan::pdl_wait();
 
   if (warp == kProducerWarp) {
     if (lane == 0) {
@@ -360,6 +364,8 @@ __device__ __forceinline__ void split1(float x, float& hi, float& lo) {
 __global__ void split_rows_kernel(const float* __restrict__ x, int cols, int64_t ldx,
                                   float* __restrict__ hi, float* __restrict__ lo, int64_t ld,
                                   bool vec) {
+  mamba_scan::pdl_trigger();
+  mamba_scan::pdl_wait();
   const int64_t r = blockIdx.y;
   const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
   if (c >= cols) return;
@@ -385,6 +391,8 @@ __global__ void split_rows_kernel(const float* __restrict__ x, int cols, int64_t
 __global__ void split_transpose_kernel(const float* __restrict__ x, int rows, int cols,
                                        int64_t ldx, float* __restrict__ hi,
                                        float* __restrict__ lo, int64_t ld) {
+  mamba_scan::pdl_trigger();
+  mamba_scan::pdl_wait();
   __shared__ float t[32][33];
   const int r0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
   const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
@@ -487,9 +495,9 @@ cudaError_t launch_gemm(const mamba_gemm::GemmMaps& maps, const mamba_gemm::Gemm
   });
   if (attr_err != cudaSuccess) return attr_err;
   const int64_t n_tiles = (p.N + C::BN - 1) / C::BN;
-  mamba_gemm::gemm_tf32x3_kernel<C><<<dim3((unsigned)m_tiles, (unsigned)n_tiles), C::kThreads,
-                                      C::kSmemBytes, st>>>(maps, p);
-  return cudaGetLastError();
+  return mamba_scan::launch_pdl(mamba_gemm::gemm_tf32x3_kernel<C>,
+                                dim3((unsigned)m_tiles, (unsigned)n_tiles), dim3(C::kThreads),
+                                C::kSmemBytes, st, maps, p);
 }
 
 bool overlap(const void* a, int64_t abytes, const void* b, int64_t bbytes) {
@@ -519,15 +527,19 @@ int mamba_split_tf32(const float* x, int64_t rows, int64_t cols, int64_t ldx, in
     const dim3 grid((unsigned)((rows + 31) / 32), (unsigned)((cols + 31) / 32));
     if (grid.y > 65535)
       return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "split_tf32: too many columns");
-    mamba_gemm::split_transpose_kernel<<<grid, dim3(32, 8), 0, st>>>(x, (int)rows, (int)cols,
-                                                                     ldx, hi, lo, ld);
+    const cudaError_t e = mamba_scan::launch_pdl(mamba_gemm::split_transpose_kernel, grid,
+                                                 dim3(32, 8), 0, st, x, (int)rows, (int)cols,
+                                                 ldx, hi, lo, ld);
+    if (e != cudaSuccess) return set_last_error(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
   } else {
     const bool vec = al16(x) && al16(hi) && al16(lo) && ldx % 4 == 0 && ld % 4 == 0;
     for (int64_t r0 = 0; r0 < rows; r0 += 65535) {  // grid.y holds at most 65535 rows
       const dim3 grid((unsigned)((cols + 4 * 128 - 1) / (4 * 128)),
                       (unsigned)std::min<int64_t>(65535, rows - r0));
-      mamba_gemm::split_rows_kernel<<<grid, 128, 0, st>>>(x + r0 * ldx, (int)cols, ldx,
-                                                          hi + r0 * ld, lo + r0 * ld, ld, vec);
+      const cudaError_t e = mamba_scan::launch_pdl(mamba_gemm::split_rows_kernel, grid, dim3(128),
+                                                   0, st, x + r0 * ldx, (int)cols, ldx,
+                                                   hi + r0 * ld, lo + r0 * ld, ld, vec);
+      if (e != cudaSuccess) return set_last_error(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
     }
   }
   const cudaError_t e = cudaGetLastError();

@@ -34,11 +34,22 @@
 
 #include "../../include/mamba_model_ops.h"
 #include "../../include/mamba_scan.h"
+#include "scan_device.cuh"
 #include "scan_kernels.h"
 
 namespace cg = cooperative_groups;
 
 namespace {
+
+using mamba_scan::launch_pdl;
+
+// Every kernel here is launched as a programmatic dependent launch: it lets
+// the next kernel be scheduled at once, then waits for the previous one
+// before its first global access.
+__device__ __forceinline__ void pdl_enter() {
+  mamba_scan::pdl_trigger();
+  mamba_scan::pdl_wait();
+}
 
 constexpr int kNormWarps = 8;        // rows per CTA of the RMSNorm kernel
 constexpr int kConvThreads = 256;    // threads per CTA of the convolution kernel
@@ -55,6 +66,7 @@ template <bool kVec>
 __global__ void __launch_bounds__(kNormWarps * 32)
     rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
                    float* __restrict__ y, int64_t rows, int cols, float eps) {
+  pdl_enter();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t r = (int64_t)blockIdx.x * kNormWarps + warp;
   if (r >= rows) return;
@@ -97,6 +109,7 @@ __global__ void __launch_bounds__(kConvThreads)
                      const float* __restrict__ w, const float* __restrict__ bias,
                      float* __restrict__ y, int64_t dim, int64_t seqlen, int64_t blocks_per_row,
                      int64_t n_items, int width) {
+  pdl_enter();
   const int64_t i = (int64_t)blockIdx.x * kConvThreads + threadIdx.x;
   if (i >= n_items) return;
   const int64_t row = i / blocks_per_row;  // b * dim + d
@@ -143,6 +156,7 @@ __global__ void __launch_bounds__(kConvThreads)
     conv_step_kernel(float* __restrict__ state, const float* __restrict__ x, int64_t x_bstride,
                      const float* __restrict__ w, const float* __restrict__ bias,
                      float* __restrict__ y, int64_t batch, int64_t dim, int width) {
+  pdl_enter();
   const int64_t i = (int64_t)blockIdx.x * kConvThreads + threadIdx.x;
   if (i >= batch * dim) return;
   const int64_t b = i / dim, d = i - b * dim;
@@ -173,6 +187,7 @@ __global__ void __launch_bounds__(kNgThreads)
     norm_gemv_kernel(const float* __restrict__ x, const float* __restrict__ norm_w,
                      const float* __restrict__ weight, float* __restrict__ out, int cols,
                      int rows_out, float eps) {
+  pdl_enter();
   __shared__ __align__(16) float xn[kNgMaxCols];
   __shared__ float red[kNgThreads / 32];
   const int b = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -228,6 +243,7 @@ __global__ void __launch_bounds__(kSsmThreads)
                     const float* __restrict__ dt_bias, const float* __restrict__ A,
                     const float* __restrict__ Dskip, float* __restrict__ state,
                     float* __restrict__ y, int dim, int rank) {
+  pdl_enter();
   __shared__ float sdt[kSsmMaxRank];
   __shared__ float sB[kSsmN], sC[kSsmN];
   const int b = blockIdx.y;
@@ -285,6 +301,7 @@ __global__ void __cluster_dims__(kXpCluster, 1, 1) __launch_bounds__(kXpThreads)
     xproj_kernel(const float* __restrict__ x, const float* __restrict__ w, float* __restrict__ dt,
                  float* __restrict__ Bm, float* __restrict__ Cm, int dim, int seqlen, int rank,
                  int dstate) {
+  pdl_enter();
   extern __shared__ __align__(16) uint8_t xp_raw[];
   XpSmem& sm = *reinterpret_cast<XpSmem*>(xp_raw);
   cg::cluster_group cluster = cg::this_cluster();
@@ -370,6 +387,7 @@ __global__ void __launch_bounds__(256)
     xproj_few_kernel(const float* __restrict__ x, const float* __restrict__ w,
                      float* __restrict__ dt, float* __restrict__ Bm, float* __restrict__ Cm,
                      int dim, int seqlen, int rank, int dstate) {
+  pdl_enter();
   __shared__ float part[2][4];
   const int P = rank + 2 * dstate;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -422,9 +440,8 @@ cudaError_t launch_xproj(dim3 grid, cudaStream_t st, const float* x, const float
                                 (int)kXpSmemBytes);
   });
   if (attr != cudaSuccess) return attr;
-  xproj_kernel<kOut><<<grid, kXpThreads, kXpSmemBytes, st>>>(x, w, dt, Bm, Cm, dim, seqlen, rank,
-                                                              dstate);
-  return cudaGetLastError();
+  return launch_pdl(xproj_kernel<kOut>, grid, dim3(kXpThreads), kXpSmemBytes, st, x, w, dt, Bm, Cm,
+                    dim, seqlen, rank, dstate);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -457,11 +474,11 @@ int mamba_rmsnorm(const float* x, const float* weight, float* y, int64_t rows, i
   const unsigned grid = (unsigned)((rows + kNormWarps - 1) / kNormWarps);
   const bool vec = cols % 4 == 0 && aligned16(x) && aligned16(weight) && aligned16(y);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (vec)
-    rmsnorm_kernel<true><<<grid, kNormWarps * 32, 0, st>>>(x, weight, y, rows, (int)cols, eps);
-  else
-    rmsnorm_kernel<false><<<grid, kNormWarps * 32, 0, st>>>(x, weight, y, rows, (int)cols, eps);
-  const cudaError_t e = cudaGetLastError();
+  const cudaError_t e =
+      vec ? launch_pdl(rmsnorm_kernel<true>, dim3(grid), dim3(kNormWarps * 32), 0, st, x, weight,
+                       y, rows, (int)cols, eps)
+          : launch_pdl(rmsnorm_kernel<false>, dim3(grid), dim3(kNormWarps * 32), 0, st, x, weight,
+                       y, rows, (int)cols, eps);
   if (e != cudaSuccess) return set_last_error(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
   return MAMBA_SCAN_OK;
 }
@@ -493,15 +510,13 @@ int mamba_causal_conv1d_silu(const float* x, int64_t x_batch_stride, const float
   const unsigned grid = (unsigned)((n_items + kConvThreads - 1) / kConvThreads);
   const bool vec = seqlen % 4 == 0 && x_batch_stride % 4 == 0 && aligned16(x) && aligned16(y);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (vec)
-    conv_silu_kernel<true><<<grid, kConvThreads, 0, st>>>(x, x_batch_stride, weight, bias, y, dim,
-                                                          seqlen, blocks_per_row, n_items,
-                                                          (int)width);
-  else
-    conv_silu_kernel<false><<<grid, kConvThreads, 0, st>>>(x, x_batch_stride, weight, bias, y,
-                                                           dim, seqlen, blocks_per_row, n_items,
-                                                           (int)width);
-  const cudaError_t e = cudaGetLastError();
+  const cudaError_t e =
+      vec ? launch_pdl(conv_silu_kernel<true>, dim3(grid), dim3(kConvThreads), 0, st, x,
+                       x_batch_stride, weight, bias, y, dim, seqlen, blocks_per_row, n_items,
+                       (int)width)
+          : launch_pdl(conv_silu_kernel<false>, dim3(grid), dim3(kConvThreads), 0, st, x,
+                       x_batch_stride, weight, bias, y, dim, seqlen, blocks_per_row, n_items,
+                       (int)width);
   if (e != cudaSuccess) return set_last_error(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
   return MAMBA_SCAN_OK;
 }
@@ -535,9 +550,8 @@ int mamba_x_proj(const float* x, const float* weight, float* dt, float* B, float
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (batch * seqlen <= kXpFewTokens) {
     const dim3 few((unsigned)((rank + 2 * dstate + 1) / 2), (unsigned)(batch * seqlen));
-    xproj_few_kernel<<<few, 256, 0, st>>>(x, weight, dt, B, C, (int)dim, (int)seqlen, (int)rank,
-                                          (int)dstate);
-    const cudaError_t e = cudaGetLastError();
+    const cudaError_t e = launch_pdl(xproj_few_kernel, few, dim3(256), 0, st, x, weight, dt, B, C,
+                                     (int)dim, (int)seqlen, (int)rank, (int)dstate);
     if (e != cudaSuccess) return set_last_error(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
     return MAMBA_SCAN_OK;
   }
@@ -571,9 +585,10 @@ int mamba_causal_conv1d_step(float* state, const float* x, int64_t x_batch_strid
   if (overlap(y, yb, state, sb) || overlap(y, yb, x, xb) || overlap(state, sb, x, xb))
     return set_last_error(MAMBA_SCAN_ERR_ALIASING, "causal_conv1d_step: buffers overlap");
   const unsigned grid = (unsigned)((batch * dim + kConvThreads - 1) / kConvThreads);
-  conv_step_kernel<<<grid, kConvThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      state, x, x_batch_stride, weight, bias, y, batch, dim, (int)width);
-  const cudaError_t e = cudaGetLastError();
+  const cudaError_t e =
+      launch_pdl(conv_step_kernel, dim3(grid), dim3(kConvThreads), 0,
+                 static_cast<cudaStream_t>(stream), state, x, x_batch_stride, weight, bias, y,
+                 batch, dim, (int)width);
   if (e != cudaSuccess) return set_last_error(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
   return MAMBA_SCAN_OK;
 }
@@ -609,9 +624,10 @@ int mamba_ssm_decode_step(const float* u, const float* z, int64_t z_batch_stride
   if (overlap(y, yb, state, sb))
     return set_last_error(MAMBA_SCAN_ERR_ALIASING, "ssm_decode_step: y overlaps state");
   const dim3 grid((unsigned)((dim + kSsmThreads - 1) / kSsmThreads), (unsigned)batch);
-  ssm_step_kernel<<<grid, kSsmThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      u, z, z_batch_stride, dt, B, C, dt_weight, dt_bias, A, D, state, y, (int)dim, (int)rank);
-  const cudaError_t e = cudaGetLastError();
+  const cudaError_t e =
+      launch_pdl(ssm_step_kernel, grid, dim3(kSsmThreads), 0, static_cast<cudaStream_t>(stream),
+                 u, z, z_batch_stride, dt, B, C, dt_weight, dt_bias, A, D, state, y, (int)dim,
+                 (int)rank);
   if (e != cudaSuccess) return set_last_error(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
   return MAMBA_SCAN_OK;
 }
@@ -635,9 +651,9 @@ int mamba_rmsnorm_gemv(const float* x, const float* norm_weight, float eps, cons
       overlap(out, ob, norm_weight, (size_t)cols * 4))
     return set_last_error(MAMBA_SCAN_ERR_ALIASING, "rmsnorm_gemv: out overlaps an input");
   const dim3 grid((unsigned)((rows_out + kNgThreads / 32 - 1) / (kNgThreads / 32)), (unsigned)batch);
-  norm_gemv_kernel<<<grid, kNgThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      x, norm_weight, weight, out, (int)cols, (int)rows_out, eps);
-  const cudaError_t e = cudaGetLastError();
+  const cudaError_t e =
+      launch_pdl(norm_gemv_kernel, grid, dim3(kNgThreads), 0, static_cast<cudaStream_t>(stream),
+                 x, norm_weight, weight, out, (int)cols, (int)rows_out, eps);
   if (e != cudaSuccess) return set_last_error(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
   return MAMBA_SCAN_OK;
 }

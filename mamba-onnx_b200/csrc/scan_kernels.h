@@ -6,6 +6,7 @@
 #include <stdint.h>
 
 #include <string>
+#include <utility>
 
 namespace mamba_scan {
 
@@ -73,6 +74,28 @@ int set_last_error(int status, const std::string& msg);
 
 // Device error word accessors (see mamba_scan_check_device_error).
 cudaError_t read_and_clear_device_error(int* code);
+
+// Enqueue `kernel` on `st` as a programmatic dependent launch: its CTAs may
+// be scheduled once every CTA of the previous kernel in the stream has
+// started (or called griddepcontrol.launch_dependents), and it must call
+// griddepcontrol.wait before touching global memory that the previous
+// kernels read or write. The model kernels (mamba_model_ops.h) all do, at
+// their top (the GEMM after its shared-memory and TMEM set-up).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 }  // namespace mamba_scan
 
