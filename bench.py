@@ -916,9 +916,9 @@ def run_decode(args):
                     "d2h_bytes_per_step": host_next.numel() * 8, "ms_per_step": e2e_ms,
                     "path": "pinned token ids -> graph replay -> argmax token to host"},
             # this package's kernels per token: per block RMSNorm + in_proj,
-            # the convolution step, x_proj and the fused dt_proj + scan step;
-            # then the final RMSNorm
-            "gpu_launches": (model.cfg.n_layer * 4 + 1) * args.steps,
+            # the convolution step, x_proj, the fused dt_proj + scan step and
+            # out_proj + residual; then the final RMSNorm + LM head
+            "gpu_launches": (model.cfg.n_layer * 5 + 1) * args.steps,
             "clocks": clocks.summary()}), flush=True)
     if world > 1:
         del graph

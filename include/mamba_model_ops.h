@@ -74,6 +74,18 @@ MAMBA_SCAN_API int mamba_rmsnorm_gemv(const float* x, const float* norm_weight, 
                                       int64_t cols, int64_t rows_out, void* stream);
 
 /*
+ * Matrix-vector product with an optional residual, for a few tokens (a
+ * block's out_proj when decoding):
+ *   out[b, j] = residual[b, j] + sum_c weight[j, c] * x[b, c]
+ * x [batch][cols], weight [rows_out][cols] (16-byte aligned), residual and
+ * out [batch][rows_out] (residual NULL for none, or out itself); out must
+ * not overlap x or weight; cols a multiple of 4, at most 4096.
+ */
+MAMBA_SCAN_API int mamba_gemv(const float* x, const float* weight, const float* residual,
+                              float* out, int64_t batch, int64_t cols, int64_t rows_out,
+                              void* stream);
+
+/*
  * One decoding step of a Mamba block's SSM, dt_proj included: for each
  * channel (b, d), with u = u[b, d] (the convolution output) and z = z[b, d]
  * (z_batch_stride floats between batch entries),

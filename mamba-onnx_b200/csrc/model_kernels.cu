@@ -223,6 +223,37 @@ __global__ void __launch_bounds__(kNgThreads)
   if (lane == 0) out[(int64_t)b * rows_out + j] = acc;
 }
 
+// out[b, j] = (residual[b, j] +) weight[j] . x[b], for a few tokens: each
+// CTA stages its token's x in shared memory, each warp takes output rows j
+// (float4 loads of weight[j], a fixed shuffle tree: deterministic).
+__global__ void __launch_bounds__(kNgThreads)
+    gemv_kernel(const float* __restrict__ x, const float* __restrict__ weight,
+                const float* __restrict__ residual, float* __restrict__ out, int cols,
+                int rows_out) {
+  pdl_enter();
+  __shared__ __align__(16) float xs[kNgMaxCols];
+  const int b = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int c = threadIdx.x; c < cols; c += kNgThreads) xs[c] = __ldg(x + (int64_t)b * cols + c);
+  __syncthreads();
+  const int j = blockIdx.x * (kNgThreads / 32) + warp;
+  if (j >= rows_out) return;
+  const float* wr = weight + (int64_t)j * cols;
+  float acc = 0.f;
+  for (int c = lane * 4; c < cols; c += 128) {
+    const float4 wv = __ldg(reinterpret_cast<const float4*>(wr + c));
+    const float4 xv = *reinterpret_cast<const float4*>(&xs[c]);
+    acc = fmaf(wv.x, xv.x, acc);
+    acc = fmaf(wv.y, xv.y, acc);
+    acc = fmaf(wv.z, xv.z, acc);
+    acc = fmaf(wv.w, xv.w, acc);
+  }
+  acc = warp_sum(acc);
+  if (lane == 0) {
+    const int64_t o = (int64_t)b * rows_out + j;
+    out[o] = residual ? residual[o] + acc : acc;
+  }
+}
+
 // ------------------------------------------------------- SSM decode step
 
 constexpr int kSsmThreads = 128;  // channels per CTA
@@ -654,6 +685,32 @@ int mamba_rmsnorm_gemv(const float* x, const float* norm_weight, float eps, cons
   const cudaError_t e =
       launch_pdl(norm_gemv_kernel, grid, dim3(kNgThreads), 0, static_cast<cudaStream_t>(stream),
                  x, norm_weight, weight, out, (int)cols, (int)rows_out, eps);
+  if (e != cudaSuccess) return set_last_error(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
+  return MAMBA_SCAN_OK;
+}
+
+int mamba_gemv(const float* x, const float* weight, const float* residual, float* out,
+               int64_t batch, int64_t cols, int64_t rows_out, void* stream) {
+  using mamba_scan::set_last_error;
+  if (batch < 0 || cols < 1 || cols > kNgMaxCols || cols % 4 != 0 || rows_out < 0)
+    return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT,
+                          "gemv: cols must be a multiple of 4 in 4.." + std::to_string(kNgMaxCols));
+  if (batch == 0 || rows_out == 0) return MAMBA_SCAN_OK;
+  if (!x || !weight || !out)
+    return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "gemv: NULL pointer");
+  if (!aligned16(weight) || batch > 65535 || rows_out > ((int64_t)1 << 30))
+    return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT,
+                          "gemv: weight must be 16-byte aligned; or too large");
+  const size_t ob = (size_t)(batch * rows_out) * 4;
+  if (overlap(out, ob, x, (size_t)(batch * cols) * 4) ||
+      overlap(out, ob, weight, (size_t)(rows_out * cols) * 4) ||
+      (residual && residual != out && overlap(out, ob, residual, ob)))
+    return set_last_error(MAMBA_SCAN_ERR_ALIASING,
+                          "gemv: out overlaps x or weight (residual may be out itself)");
+  const dim3 grid((unsigned)((rows_out + kNgThreads / 32 - 1) / (kNgThreads / 32)), (unsigned)batch);
+  const cudaError_t e =
+      launch_pdl(gemv_kernel, grid, dim3(kNgThreads), 0, static_cast<cudaStream_t>(stream), x,
+                 weight, residual, out, (int)cols, (int)rows_out);
   if (e != cudaSuccess) return set_last_error(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
   return MAMBA_SCAN_OK;
 }

@@ -86,6 +86,8 @@ def library() -> ctypes.CDLL:
         lib.mamba_rmsnorm_gemv.restype = ctypes.c_int
         lib.mamba_rmsnorm_gemv.argtypes = [ctypes.c_void_p] * 2 + [ctypes.c_float] + \
             [ctypes.c_void_p] * 2 + [ctypes.c_int64] * 3 + [ctypes.c_void_p]
+        lib.mamba_gemv.restype = ctypes.c_int
+        lib.mamba_gemv.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int64] * 3 + [ctypes.c_void_p]
         lib.mamba_ssm_decode_step.restype = ctypes.c_int
         lib.mamba_ssm_decode_step.argtypes = [ctypes.c_void_p] * 2 + [ctypes.c_int64] + \
             [ctypes.c_void_p] * 9 + [ctypes.c_int64] * 4 + [ctypes.c_void_p]
@@ -306,6 +308,25 @@ def rmsnorm_gemv(x, norm_weight, eps: float, weight, stream=None):
                                       _ptr(out), batch, cols, rows_out, st.cuda_stream)
     if rc != STATUS_OK:
         _raise(rc, "rmsnorm_gemv")
+    return out
+
+
+def gemv(x, weight, residual=None, stream=None):
+    """(residual +) x @ weight.T for a few tokens: x [batch, cols], weight
+    [rows_out, cols], residual [batch, rows_out] or None -> [batch, rows_out]."""
+    import torch
+
+    batch, cols = x.shape
+    rows_out = weight.shape[0]
+    _check("x", x, (batch, cols))
+    _check("weight", weight, (rows_out, cols))
+    _check("residual", residual, (batch, rows_out))
+    out = torch.empty(batch, rows_out, dtype=torch.float32, device=x.device)
+    st = stream if stream is not None else torch.cuda.current_stream(x.device)
+    rc = library().mamba_gemv(_ptr(x), _ptr(weight), _ptr(residual), _ptr(out), batch, cols,
+                              rows_out, st.cuda_stream)
+    if rc != STATUS_OK:
+        _raise(rc, "gemv")
     return out
 
 

@@ -207,9 +207,9 @@ class MambaLayer(torch.nn.Module):
         D, N, R = self.cfg.d_inner, self.cfg.d_state, self.cfg.rank
         if h.is_cuda:
             # this package's kernels: RMSNorm + in_proj, the convolution step
-            # (window shift, conv, SiLU), x_proj, then dt_proj + the scan step
-            # + the state update in one kernel (SelectiveScanFusedExact at
-            # seqlen 1)
+            # (window shift, conv, SiLU), x_proj, dt_proj + the scan step + the
+            # state update in one kernel (SelectiveScanFusedExact at seqlen 1),
+            # then out_proj + the residual
             xz = cuda.rmsnorm_gemv(h[:, 0], self.norm_weight.detach(), self.cfg.rms_eps,
                                    self.in_proj_weight.detach()).unsqueeze(-1)  # [B, 2D, 1]
             x = cuda.causal_conv1d_step(conv_state, xz[:, :D, 0], self.conv_weight.detach(),
@@ -218,7 +218,7 @@ class MambaLayer(torch.nn.Module):
             y = cuda.ssm_decode_step(x, xz[:, D:, 0], dt[:, 0], Bm[:, 0], Cm[:, 0],
                                      self.dt_proj_weight.detach(), self.dt_proj_bias.detach(),
                                      A, self.D.detach(), ssm_state)
-            return add_out_proj(h, y.unsqueeze(-1), self.out_proj_weight)
+            return cuda.gemv(y, self.out_proj_weight.detach(), residual=h[:, 0]).unsqueeze(1)
         # the same step in torch operations around the scan op
         xz = self._in_proj(h)  # [B, 2D, 1]
         conv_state.copy_(torch.cat([conv_state[..., 1:], xz[:, :D]], dim=-1))
@@ -342,6 +342,9 @@ class MambaLM(torch.nn.Module):
         h = F.embedding(input_ids[:, None], self.embedding)
         for layer, cs, ss in zip(self.layers, state.conv, state.ssm):
             h = layer.step(h, layer.A(), cs, ss)
+        if h.is_cuda:  # final RMSNorm and the tied LM head in one kernel
+            return cuda.rmsnorm_gemv(h[:, 0], self.norm_f_weight.detach(), self.cfg.rms_eps,
+                                     self.embedding.detach())
         return self._head(h)[:, 0]
 
     @torch.no_grad()

@@ -174,6 +174,16 @@ def test_rmsnorm_gemv_validates_before_launch():
     assert lib.mamba_rmsnorm_gemv(f, 2 * f, 1e-5, 3 * f, 4 * f, 0, 64, 8, None) == 0
 
 
+def test_gemv_validates_before_launch():
+    lib = cuda.library()
+    f = 0x100000
+    assert lib.mamba_gemv(f, 2 * f, None, 3 * f, 1, 66, 8, None) == 1
+    assert lib.mamba_gemv(f, 2 * f + 4, None, 3 * f, 1, 64, 8, None) == 1
+    assert lib.mamba_gemv(f, 2 * f, None, f + 8, 1, 64, 8, None) == 4
+    assert lib.mamba_gemv(f, 2 * f, 3 * f + 4, 3 * f, 1, 64, 8, None) == 4  # partial overlap
+    assert lib.mamba_gemv(f, 2 * f, None, 3 * f, 0, 64, 8, None) == 0
+
+
 def test_x_proj_validates_before_launch():
     lib = cuda.library()
     f = 0x100000

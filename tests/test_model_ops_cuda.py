@@ -179,3 +179,16 @@ def test_rmsnorm_gemv_matches_float64(batch, cols, rows):
     ref = hn @ w.double().t()
     assert float((got.double() - ref).norm() / ref.norm()) < 1e-6
     assert torch.equal(got, cuda.rmsnorm_gemv(x, nw, 1e-5, w))
+
+
+@pytest.mark.parametrize("batch,cols,rows,res", [(1, 1536, 768, True), (3, 64, 10, False),
+                                                 (2, 768, 50280, False)])
+def test_gemv_matches_float64(batch, cols, rows, res):
+    """(residual +) W x for decoding tokens (out_proj, the LM head) against float64."""
+    g = torch.Generator(device="cpu").manual_seed(cols + rows)
+    x = torch.randn(batch, cols, generator=g).cuda()
+    w = (torch.randn(rows, cols, generator=g) * 0.02).cuda()
+    r = torch.randn(batch, rows, generator=g).cuda() if res else None
+    got = cuda.gemv(x, w, residual=r)
+    ref = x.double() @ w.double().t() + (r.double() if res else 0)
+    assert float((got.double() - ref).norm() / ref.norm()) < 1e-6
