@@ -287,8 +287,23 @@ __global__ void __launch_bounds__(kSsmThreads)
   const int d = blockIdx.x * kSsmThreads + threadIdx.x;
   if (d >= dim) return;
   const float* wr = w_dt + (int64_t)d * rank;
-  float xd = dt_bias ? __ldg(dt_bias + d) : 0.f;
-  for (int r = 0; r < rank; ++r) xd = fmaf(__ldg(wr + r), sdt[r], xd);
+  // W_dt[d] . dt: float4 loads of the row (all in flight), four partial sums
+  float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+  int r = 0;
+  if ((rank & 3) == 0 && (reinterpret_cast<uintptr_t>(w_dt) & 15u) == 0) {
+    const float4* w4 = reinterpret_cast<const float4*>(wr);
+#pragma unroll 4
+    for (int q = 0; q < rank / 4; ++q) {
+      const float4 wv = __ldg(w4 + q);
+      a0 = fmaf(wv.x, sdt[4 * q], a0);
+      a1 = fmaf(wv.y, sdt[4 * q + 1], a1);
+      a2 = fmaf(wv.z, sdt[4 * q + 2], a2);
+      a3 = fmaf(wv.w, sdt[4 * q + 3], a3);
+    }
+    r = rank;
+  }
+  for (; r < rank; ++r) a0 = fmaf(__ldg(wr + r), sdt[r], a0);
+  const float xd = (dt_bias ? __ldg(dt_bias + d) : 0.f) + ((a0 + a1) + (a2 + a3));
   const float e = expf(xd);
   const float delta = xd > 20.f ? xd : (xd < -20.f ? e : log1pf(e));
   const int64_t row = (int64_t)b * dim + d;
