@@ -111,8 +111,11 @@ MAMBA_SCAN_API int mamba_scan_launch(int variant, const mamba_scan_args* args, v
  *
  * - Shapes that need more scratch than that (see mamba_scan_workspace_size)
  *   are rejected with MAMBA_SCAN_ERR_WORKSPACE; nothing is enqueued.
- * - The first call on a device looks up the array's address on that device
- *   (cudaGetSymbolAddress), so make it before any stream capture.
+ * - Every call looks up the array's address in the CUDA context current on
+ *   the calling thread (cudaGetSymbolAddress: a host-side query that
+ *   allocates nothing), so a context that changes under the same device index
+ *   never receives a stale address. The first call on a device also loads the
+ *   library's kernels there: make one call before any stream capture.
  * - Every call on a device uses the same array. Calls whose work can overlap
  *   on the GPU (different streams without ordering between them, several
  *   host threads) race on it; order them on one stream. No call depends on

@@ -226,10 +226,12 @@ __global__ void __launch_bounds__(kNgThreads)
 // out[b, j] = (residual[b, j] +) weight[j] . x[b], for a few tokens: each
 // CTA stages its token's x in shared memory, each warp takes output rows j
 // (float4 loads of weight[j], a fixed shuffle tree: deterministic).
+// residual may be out itself (the residual stream updated in place), so
+// neither is declared __restrict__: each output element's residual is read by
+// the lane that then writes it.
 __global__ void __launch_bounds__(kNgThreads)
     gemv_kernel(const float* __restrict__ x, const float* __restrict__ weight,
-                const float* __restrict__ residual, float* __restrict__ out, int cols,
-                int rows_out) {
+                const float* residual, float* out, int cols, int rows_out) {
   pdl_enter();
   __shared__ __align__(16) float xs[kNgMaxCols];
   const int b = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;

@@ -13,20 +13,82 @@
 // * shapes, ranks, element types and dstate are validated before any launch;
 // * SelectiveScanFused / SelectiveScanFusedExact accept an OPTIONAL 8th input,
 //   delta_bias [D], added to delta before softplus; 7-input graphs are unchanged;
-// * scratch for the chunked long-sequence path comes from the context's
-//   allocator for the output's memory (freed right after the launch; ORT's
-//   stream-ordered arena keeps it valid for work already enqueued).
+// * scratch for the chunked long-sequence path is a per-kernel buffer for
+//   each (device, stream) the kernel is run on, taken from the context's
+//   allocator for the output's memory the first time it is needed, grown when
+//   a larger shape needs more, and returned to that allocator in
+//   KernelDestroy. A buffer is only ever used by work on its own stream, so
+//   concurrent runs on different streams (ORT's multi-stream execution,
+//   several sessions threads) never share scratch, and runs on one stream
+//   are ordered by the stream itself; an outgrown buffer is kept until
+//   KernelDestroy because work already enqueued may still read it.
 //
-// Compiles against the real onnxruntime_c_api.h or the stand-in in csrc/ort.
+// Compiles against the real onnxruntime_c_api.h or the one in csrc/ort, which
+// has ONNX Runtime's slot order (checked below).
+#include <cuda_runtime.h>
+
+#include <cstddef>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "onnxruntime_c_api.h"
 
 #include "../../include/mamba_ops_cuda.h"
 #include "../../include/mamba_scan.h"
+
+// OrtApi slot indices: the last entry of each API version's block (the
+// counts ONNX Runtime asserts for its own table) and every entry called here.
+#define MAMBA_ORT_SLOT(member, index)                                             \
+  static_assert(offsetof(OrtApi, member) / sizeof(void*) == (index),               \
+                "OrtApi::" #member " must be slot " #index " of ONNX Runtime's table")
+MAMBA_ORT_SLOT(ReleaseCustomOpDomain, 101);
+MAMBA_ORT_SLOT(ReleaseModelMetadata, 118);
+MAMBA_ORT_SLOT(AddFreeDimensionOverrideByName, 124);
+MAMBA_ORT_SLOT(ReleaseAvailableProviders, 126);
+MAMBA_ORT_SLOT(SetGlobalSpinControl, 149);
+MAMBA_ORT_SLOT(ReleaseArenaCfg, 157);
+MAMBA_ORT_SLOT(GetCurrentGpuDeviceId, 161);
+MAMBA_ORT_SLOT(CreateSessionFromArrayWithPrepackedWeightsContainer, 169);
+MAMBA_ORT_SLOT(GetSparseTensorIndices, 191);
+MAMBA_ORT_SLOT(SynchronizeBoundOutputs, 203);
+MAMBA_ORT_SLOT(SessionOptionsAppendExecutionProvider_MIGraphX, 209);
+MAMBA_ORT_SLOT(ReleaseKernelInfo, 218);
+MAMBA_ORT_SLOT(ReleaseCANNProviderOptions, 224);
+MAMBA_ORT_SLOT(GetSessionConfigEntry, 238);
+MAMBA_ORT_SLOT(GetBuildInfoString, 254);
+MAMBA_ORT_SLOT(KernelContext_GetResource, 265);
+MAMBA_ORT_SLOT(SessionOptionsAppendExecutionProvider_OpenVINO_V2, 275);
+MAMBA_ORT_SLOT(CreateStatus, 0);
+MAMBA_ORT_SLOT(GetErrorCode, 1);
+MAMBA_ORT_SLOT(GetErrorMessage, 2);
+MAMBA_ORT_SLOT(CreateCustomOpDomain, 26);
+MAMBA_ORT_SLOT(CustomOpDomain_Add, 27);
+MAMBA_ORT_SLOT(AddCustomOpDomain, 28);
+MAMBA_ORT_SLOT(GetTensorMutableData, 51);
+MAMBA_ORT_SLOT(GetTensorElementType, 60);
+MAMBA_ORT_SLOT(GetDimensionsCount, 61);
+MAMBA_ORT_SLOT(GetDimensions, 62);
+MAMBA_ORT_SLOT(GetTensorTypeAndShape, 65);
+MAMBA_ORT_SLOT(KernelContext_GetInputCount, 88);
+MAMBA_ORT_SLOT(KernelContext_GetOutputCount, 89);
+MAMBA_ORT_SLOT(KernelContext_GetInput, 90);
+MAMBA_ORT_SLOT(KernelContext_GetOutput, 91);
+MAMBA_ORT_SLOT(ReleaseStatus, 93);
+MAMBA_ORT_SLOT(ReleaseTensorTypeAndShapeInfo, 99);
+MAMBA_ORT_SLOT(ReleaseAllocator, 132);
+MAMBA_ORT_SLOT(KernelContext_GetGPUComputeStream, 193);
+MAMBA_ORT_SLOT(GetTensorMemoryInfo, 194);
+MAMBA_ORT_SLOT(KernelContext_GetAllocator, 253);
+#undef MAMBA_ORT_SLOT
+// OrtCustomOp member order (the table ORT reads, up to version 17).
+static_assert(offsetof(OrtCustomOp, CreateKernel) == sizeof(void*), "OrtCustomOp layout");
+static_assert(offsetof(OrtCustomOp, KernelCompute) == 8 * sizeof(void*), "OrtCustomOp layout");
+static_assert(offsetof(OrtCustomOp, GetInputMemoryType) == 12 * sizeof(void*), "OrtCustomOp layout");
+static_assert(offsetof(OrtCustomOp, CreateKernelV2) == 17 * sizeof(void*), "OrtCustomOp layout");
+static_assert(offsetof(OrtCustomOp, GetEndVersion) == 21 * sizeof(void*), "OrtCustomOp layout");
 
 namespace {
 
@@ -50,19 +112,61 @@ struct ScanOp {
   const OpDesc* desc;
 };
 
-struct ScanKernel {
-  const OrtApi* api;
-  const OpDesc* desc;
-};
-
-const OpDesc* desc_of(const OrtCustomOp* op) { return reinterpret_cast<const ScanOp*>(op)->desc; }
-
 // Runs an ORT call; on failure returns its status from the enclosing function.
 #define MAMBA_ORT_TRY(expr)                 \
   do {                                      \
     OrtStatus* mamba_status_ = (expr);      \
     if (mamba_status_) return mamba_status_; \
   } while (0)
+
+// Scratch of one kernel on one (device, stream).
+struct Scratch {
+  int device;
+  void* stream;
+  void* ptr;
+  size_t bytes;
+};
+
+struct ScanKernel {
+  const OrtApi* api;
+  const OpDesc* desc;
+  std::mutex mu;                 // held from scratch lookup to the end of the launch
+  OrtAllocator* alloc = nullptr;  // released in KernelDestroy
+  std::vector<Scratch> scratch;
+  std::vector<void*> retired;    // outgrown buffers: enqueued work may still read them
+};
+
+// The kernel's scratch for (device, stream), at least `bytes` long; taken from
+// (or grown through) the context's allocator for the output's memory. Called
+// with k.mu held.
+OrtStatus* scratch_for(const OrtApi& api, ScanKernel& k, OrtKernelContext* ctx, OrtValue* out_v,
+                       int device, void* stream, size_t bytes, void** ptr) {
+  Scratch* s = nullptr;
+  for (auto& e : k.scratch)
+    if (e.device == device && e.stream == stream) s = &e;
+  if (s != nullptr && s->bytes >= bytes) {
+    *ptr = s->ptr;
+    return nullptr;
+  }
+  if (k.alloc == nullptr) {
+    const OrtMemoryInfo* mem = nullptr;
+    MAMBA_ORT_TRY(api.GetTensorMemoryInfo(out_v, &mem));
+    MAMBA_ORT_TRY(api.KernelContext_GetAllocator(ctx, mem, &k.alloc));
+  }
+  void* p = k.alloc->Alloc(k.alloc, bytes);
+  if (p == nullptr) return api.CreateStatus(ORT_RUNTIME_EXCEPTION, "scan workspace allocation failed");
+  if (s != nullptr) {
+    k.retired.push_back(s->ptr);
+    s->ptr = p;
+    s->bytes = bytes;
+  } else {
+    k.scratch.push_back(Scratch{device, stream, p, bytes});
+  }
+  *ptr = p;
+  return nullptr;
+}
+
+const OpDesc* desc_of(const OrtCustomOp* op) { return reinterpret_cast<const ScanOp*>(op)->desc; }
 
 struct TensorView {
   const OrtValue* value = nullptr;
@@ -95,7 +199,9 @@ std::string shape_str(const TensorView& t) {
   return s + "]";
 }
 
-OrtStatus* compute(const OrtApi& api, const OpDesc& op, OrtKernelContext* ctx) {
+OrtStatus* compute(ScanKernel& k, OrtKernelContext* ctx) {
+  const OrtApi& api = *k.api;
+  const OpDesc& op = *k.desc;
   size_t n_in = 0;
   MAMBA_ORT_TRY(api.KernelContext_GetInputCount(ctx, &n_in));
   if (n_in < op.n_required || n_in > op.n_total)
@@ -164,24 +270,21 @@ OrtStatus* compute(const OrtApi& api, const OpDesc& op, OrtKernelContext* ctx) {
   a.seqlen = seqlen;
   a.dstate = dstate;
 
-  // Workspace for the chunked path, from the allocator of the output's memory.
+  // Scratch for the chunked path: this kernel's buffer for (device, stream).
   const size_t ws_bytes = mamba_scan_workspace_size(op.variant, batch, dim, seqlen, dstate);
-  OrtAllocator* alloc = nullptr;
-  void* ws = nullptr;
+  int rc = MAMBA_SCAN_OK;
   if (ws_bytes > 0) {
-    const OrtMemoryInfo* mem = nullptr;
-    MAMBA_ORT_TRY(api.GetTensorMemoryInfo(out_v, &mem));
-    MAMBA_ORT_TRY(api.KernelContext_GetAllocator(ctx, mem, &alloc));
-    ws = alloc->Alloc(alloc, ws_bytes);
-    if (ws == nullptr) {
-      api.ReleaseAllocator(alloc);
-      return api.CreateStatus(ORT_RUNTIME_EXCEPTION, "workspace allocation failed");
-    }
-  }
-  const int rc = mamba_scan_launch(op.variant, &a, ws, ws_bytes, stream);
-  if (alloc) {
-    alloc->Free(alloc, ws);
-    api.ReleaseAllocator(alloc);
+    int device = 0;
+    const cudaError_t ce = cudaGetDevice(&device);
+    if (ce != cudaSuccess)
+      return api.CreateStatus(ORT_RUNTIME_EXCEPTION,
+                              (std::string(op.name) + ": " + cudaGetErrorString(ce)).c_str());
+    std::lock_guard<std::mutex> lock(k.mu);
+    void* ws = nullptr;
+    MAMBA_ORT_TRY(scratch_for(api, k, ctx, out_v, device, stream, ws_bytes, &ws));
+    rc = mamba_scan_launch(op.variant, &a, ws, ws_bytes, stream);
+  } else {
+    rc = mamba_scan_launch(op.variant, &a, nullptr, 0, stream);
   }
   if (rc != MAMBA_SCAN_OK) {
     const OrtErrorCode code = (rc == MAMBA_SCAN_ERR_CUDA || rc == MAMBA_SCAN_ERR_DEVICE_TIMEOUT)
@@ -198,7 +301,10 @@ OrtStatus* compute(const OrtApi& api, const OpDesc& op, OrtKernelContext* ctx) {
 
 OrtStatusPtr ORT_API_CALL create_kernel_v2(const OrtCustomOp* op, const OrtApi* api,
                                            const OrtKernelInfo*, void** kernel) {
-  *kernel = new ScanKernel{api, desc_of(op)};
+  auto* k = new ScanKernel;
+  k->api = api;
+  k->desc = desc_of(op);
+  *kernel = k;
   return nullptr;
 }
 
@@ -210,21 +316,41 @@ void* ORT_API_CALL create_kernel(const OrtCustomOp* op, const OrtApi* api,
 }
 
 OrtStatusPtr ORT_API_CALL kernel_compute_v2(void* kernel, OrtKernelContext* ctx) {
-  auto* k = static_cast<ScanKernel*>(kernel);
-  return compute(*k->api, *k->desc, ctx);
+  return compute(*static_cast<ScanKernel*>(kernel), ctx);
 }
 
 // Entry for hosts without the V2 table slots: the status cannot be returned,
 // so it is reported on stderr (never thrown across the C ABI).
 void ORT_API_CALL kernel_compute(void* kernel, OrtKernelContext* ctx) {
   auto* k = static_cast<ScanKernel*>(kernel);
-  if (OrtStatus* s = compute(*k->api, *k->desc, ctx)) {
+  if (OrtStatus* s = compute(*k, ctx)) {
     std::fprintf(stderr, "[mamba_ops_cuda] %s\n", k->api->GetErrorMessage(s));
     k->api->ReleaseStatus(s);
   }
 }
 
-void ORT_API_CALL kernel_destroy(void* kernel) { delete static_cast<ScanKernel*>(kernel); }
+// Returns the kernel's scratch to the allocator it came from, after the work
+// on each device that may still read it has finished.
+void ORT_API_CALL kernel_destroy(void* kernel) {
+  auto* k = static_cast<ScanKernel*>(kernel);
+  if (k->alloc != nullptr) {
+    int current = 0;
+    const bool have_current = cudaGetDevice(&current) == cudaSuccess;
+    std::vector<int> synced;
+    for (const auto& e : k->scratch) {
+      bool seen = false;
+      for (int d : synced) seen = seen || d == e.device;
+      if (seen) continue;
+      synced.push_back(e.device);
+      if (cudaSetDevice(e.device) == cudaSuccess) cudaDeviceSynchronize();
+    }
+    if (have_current) cudaSetDevice(current);
+    for (const auto& e : k->scratch) k->alloc->Free(k->alloc, e.ptr);
+    for (void* p : k->retired) k->alloc->Free(k->alloc, p);
+    k->api->ReleaseAllocator(k->alloc);
+  }
+  delete k;
+}
 
 const char* ORT_API_CALL op_name(const OrtCustomOp* op) { return desc_of(op)->name; }
 const char* ORT_API_CALL op_ep(const OrtCustomOp*) { return "CUDAExecutionProvider"; }
@@ -248,13 +374,14 @@ int ORT_API_CALL op_end_version(const OrtCustomOp*) { return 2147483647; }
 
 ScanOp g_ops[4];
 std::once_flag g_ops_once;
+uint32_t g_ops_version = ORT_API_VERSION;  // the API version the runtime offered
 
 void init_ops() {
   for (int i = 0; i < 4; ++i) {
     ScanOp& s = g_ops[i];
     std::memset(&s, 0, sizeof s);
     OrtCustomOp& o = s.base;
-    o.version = ORT_API_VERSION;
+    o.version = g_ops_version;
     o.CreateKernel = create_kernel;
     o.GetName = op_name;
     o.GetExecutionProviderType = op_ep;
@@ -277,12 +404,33 @@ void init_ops() {
 
 }  // namespace
 
+// Registers the four ops with the newest OrtApi version (17, 16 or 15) the
+// runtime offers; the op tables declare that version, so an older runtime
+// reads only the members it knows (before 16: the void KernelCompute entry,
+// which reports failures on stderr). Without any usable API (no api_base, or
+// a runtime older than 15) nothing can carry a status back: the reason goes
+// to stderr and the call returns NULL with no op registered.
 extern "C" OrtStatus* ORT_API_CALL RegisterCustomOps(OrtSessionOptions* options,
                                                      const OrtApiBase* api_base) {
-  if (api_base == nullptr) return nullptr;  // nothing to report the error through
-  const OrtApi* api = api_base->GetApi(ORT_API_VERSION);
-  if (api == nullptr) return nullptr;
-  std::call_once(g_ops_once, init_ops);
+  if (api_base == nullptr) {
+    std::fprintf(stderr, "[mamba_ops_cuda] RegisterCustomOps: no OrtApiBase; ops not registered\n");
+    return nullptr;
+  }
+  const OrtApi* api = nullptr;
+  uint32_t version = ORT_API_VERSION;
+  for (; version >= 15 && api == nullptr; --version) api = api_base->GetApi(version);
+  ++version;
+  if (api == nullptr) {
+    std::fprintf(stderr,
+                 "[mamba_ops_cuda] RegisterCustomOps: ONNX Runtime %s offers no OrtApi version "
+                 "15..%d; ops not registered\n",
+                 api_base->GetVersionString ? api_base->GetVersionString() : "?", ORT_API_VERSION);
+    return nullptr;
+  }
+  std::call_once(g_ops_once, [version] {
+    g_ops_version = version;
+    init_ops();
+  });
   OrtCustomOpDomain* domain = nullptr;
   MAMBA_ORT_TRY(api->CreateCustomOpDomain("mamba", &domain));
   for (auto& op : g_ops) {

@@ -12,11 +12,14 @@
 // The array is a file-scope __device__ variable: every GPU on which the
 // library's kernels are loaded holds its own copy, MAMBA_SCAN_STATIC_WORKSPACE_BYTES
 // bytes, until the process exits. Its device address is looked up with
-// cudaGetSymbolAddress once per device, on the first call made with that
-// device current.
+// cudaGetSymbolAddress on every call, with the caller's device current: the
+// address belongs to the CUDA context the module is loaded in, which can
+// change under the same device index (after cudaDeviceReset, or for a
+// driver-API caller that makes another context current), so it is never
+// reused from an earlier call. The lookup is a host-side query that allocates
+// nothing; the first one on a device also loads the library's kernels there.
 #include <cuda_runtime.h>
 
-#include <mutex>
 #include <string>
 
 #include "../../include/mamba_scan.h"
@@ -27,25 +30,6 @@ namespace {
 // Chunk aggregates of the calls made through this entry point, shared by all
 // of them.
 static __device__ __align__(256) unsigned char g_static_workspace[MAMBA_SCAN_STATIC_WORKSPACE_BYTES];
-
-constexpr int kMaxDevices = 64;
-
-// Device address of g_static_workspace on `device` (the current device).
-// In host code the name g_static_workspace is only a handle for the runtime;
-// the address a kernel can use comes from cudaGetSymbolAddress.
-cudaError_t static_workspace_address(int device, void** out) {
-  static std::mutex mu;
-  static void* addr[kMaxDevices] = {};
-  std::lock_guard<std::mutex> lock(mu);
-  if (addr[device] == nullptr) {
-    void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_static_workspace);
-    if (e != cudaSuccess) return e;
-    addr[device] = p;
-  }
-  *out = addr[device];
-  return cudaSuccess;
-}
 
 }  // namespace
 
@@ -61,14 +45,11 @@ extern "C" int mamba_scan_launch_static_workspace(int variant, const mamba_scan_
         "this shape needs " + std::to_string(need) + " bytes of workspace; the built-in workspace " +
             "holds " + std::to_string((size_t)MAMBA_SCAN_STATIC_WORKSPACE_BYTES) +
             " (use mamba_scan_launch with a caller-provided workspace)");
-  int device = 0;
-  cudaError_t e = cudaGetDevice(&device);
-  if (e != cudaSuccess)
-    return mamba_scan::set_last_error(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
-  if (device < 0 || device >= kMaxDevices)
-    return mamba_scan::set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "device index above 63");
+  // In host code g_static_workspace only names the variable for the runtime;
+  // the address a kernel can use comes from cudaGetSymbolAddress, for the
+  // context current now.
   void* ws = nullptr;
-  e = static_workspace_address(device, &ws);
+  const cudaError_t e = cudaGetSymbolAddress(&ws, g_static_workspace);
   if (e != cudaSuccess)
     return mamba_scan::set_last_error(
         MAMBA_SCAN_ERR_CUDA, std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));

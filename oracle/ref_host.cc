@@ -129,14 +129,35 @@ OrtStatusPtr get_dims(const OrtTensorTypeAndShapeInfo* i, int64_t* d, size_t n) 
 }
 void release_type_shape(OrtTensorTypeAndShapeInfo*) {}
 
-const OrtApi kApi = {
-    make_status,   status_code,     status_msg,      release_status,
-    create_domain, domain_add,      add_domain,      release_domain,
-    get_input_count, get_output_count, get_input,    get_output,
-    get_stream,    get_allocator,   release_allocator,
-    get_data,      get_meminfo,     get_type_shape,  get_elem_type,
-    get_dim_count, get_dims,        release_type_shape,
-};
+OrtApi make_api() {
+  OrtApi a;
+  std::memset(&a, 0, sizeof a);
+  a.CreateStatus = make_status;
+  a.GetErrorCode = status_code;
+  a.GetErrorMessage = status_msg;
+  a.ReleaseStatus = release_status;
+  a.CreateCustomOpDomain = create_domain;
+  a.CustomOpDomain_Add = domain_add;
+  a.AddCustomOpDomain = add_domain;
+  a.ReleaseCustomOpDomain = release_domain;
+  a.KernelContext_GetInputCount = get_input_count;
+  a.KernelContext_GetOutputCount = get_output_count;
+  a.KernelContext_GetInput = get_input;
+  a.KernelContext_GetOutput = get_output;
+  a.KernelContext_GetGPUComputeStream = get_stream;
+  a.KernelContext_GetAllocator = get_allocator;
+  a.ReleaseAllocator = release_allocator;
+  a.GetTensorMutableData = get_data;
+  a.GetTensorMemoryInfo = get_meminfo;
+  a.GetTensorTypeAndShape = get_type_shape;
+  a.GetTensorElementType = get_elem_type;
+  a.GetDimensionsCount = get_dim_count;
+  a.GetDimensions = get_dims;
+  a.ReleaseTensorTypeAndShapeInfo = release_type_shape;
+  return a;
+}
+// Filled by member name: the layout is ONNX Runtime's (unused slots stay NULL).
+const OrtApi kApi = make_api();
 const OrtApi* get_api(uint32_t) { return &kApi; }
 const char* version_string() { return "oracle-host"; }
 const OrtApiBase kBase = {get_api, version_string};

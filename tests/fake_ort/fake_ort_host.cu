@@ -173,14 +173,35 @@ OrtStatusPtr get_dims(const OrtTensorTypeAndShapeInfo* i, int64_t* d, size_t n) 
 }
 void release_type_shape(OrtTensorTypeAndShapeInfo*) {}
 
-const OrtApi kApi = {
-    make_status,     status_code,      status_msg,    release_status,
-    create_domain,   domain_add,       add_domain,    release_domain,
-    get_input_count, get_output_count, get_input,     get_output,
-    get_stream,      get_allocator,    release_allocator,
-    get_data,        get_meminfo,      get_type_shape, get_elem_type,
-    get_dim_count,   get_dims,         release_type_shape,
-};
+OrtApi make_api() {
+  OrtApi a;
+  std::memset(&a, 0, sizeof a);
+  a.CreateStatus = make_status;
+  a.GetErrorCode = status_code;
+  a.GetErrorMessage = status_msg;
+  a.ReleaseStatus = release_status;
+  a.CreateCustomOpDomain = create_domain;
+  a.CustomOpDomain_Add = domain_add;
+  a.AddCustomOpDomain = add_domain;
+  a.ReleaseCustomOpDomain = release_domain;
+  a.KernelContext_GetInputCount = get_input_count;
+  a.KernelContext_GetOutputCount = get_output_count;
+  a.KernelContext_GetInput = get_input;
+  a.KernelContext_GetOutput = get_output;
+  a.KernelContext_GetGPUComputeStream = get_stream;
+  a.KernelContext_GetAllocator = get_allocator;
+  a.ReleaseAllocator = release_allocator;
+  a.GetTensorMutableData = get_data;
+  a.GetTensorMemoryInfo = get_meminfo;
+  a.GetTensorTypeAndShape = get_type_shape;
+  a.GetTensorElementType = get_elem_type;
+  a.GetDimensionsCount = get_dim_count;
+  a.GetDimensions = get_dims;
+  a.ReleaseTensorTypeAndShapeInfo = release_type_shape;
+  return a;
+}
+// Filled by member name: the layout is ONNX Runtime's (unused slots stay NULL).
+const OrtApi kApi = make_api();
 const OrtApi* get_api(uint32_t) { return &kApi; }
 const char* version_string() { return "fake-cuda-ep"; }
 const OrtApiBase kBase = {get_api, version_string};
@@ -257,19 +278,48 @@ void fake_ort_fail_next(const char* api_name) { g_fail_next = api_name ? api_nam
 
 int fake_ort_live_allocations(void) { return g_alloc_live; }
 
-// Run op `name` of library `lib`. ptrs[i] == NULL marks an omitted optional
-// input. dims holds the inputs' dims back to back (ranks[i] each); types[i]
-// is the ONNX element type. Returns 0 or the OrtErrorCode of the status the
-// op returned (message in err). use_v2 = 0 runs the void KernelCompute entry.
-int fake_ort_run(int lib, const char* name, int n_inputs, void* const* ptrs,
-                 const int64_t* dims, const int* ranks, const int* types, void* out,
-                 const int64_t* out_dims, int out_rank, void* stream, int use_v2, char* err,
-                 size_t err_len) {
+// A kernel created once and run any number of times, as ORT keeps one kernel
+// object per graph node for the life of a session.
+struct HostKernel {
+  const OrtCustomOp* op = nullptr;
+  void* kernel = nullptr;
+  bool v2 = false;
+};
+std::vector<HostKernel*> g_kernels;
+
+// Create a kernel of op `name`; returns a handle >= 0, or -1 (reason in err).
+int fake_ort_kernel_create(int lib, const char* name, int use_v2, char* err, size_t err_len) {
   const OrtCustomOp* op = find_op(lib, name);
   if (!op) {
     set_err(err, err_len, std::string("no op named ") + name);
-    return ORT_NOT_IMPLEMENTED;
+    return -1;
   }
+  auto* hk = new HostKernel;
+  hk->op = op;
+  hk->v2 = use_v2 && op->CreateKernelV2 && op->KernelComputeV2;
+  if (hk->v2) {
+    if (OrtStatus* s = op->CreateKernelV2(op, &kApi, nullptr, &hk->kernel)) {
+      set_err(err, err_len, status_msg(s));
+      release_status(s);
+      delete hk;
+      return -1;
+    }
+  } else {
+    hk->kernel = op->CreateKernel(op, &kApi, nullptr);
+  }
+  g_kernels.push_back(hk);
+  return (int)g_kernels.size() - 1;
+}
+
+// Run kernel `handle` once (see fake_ort_run for the arguments).
+int fake_ort_kernel_run(int handle, int n_inputs, void* const* ptrs, const int64_t* dims,
+                        const int* ranks, const int* types, void* out, const int64_t* out_dims,
+                        int out_rank, void* stream, char* err, size_t err_len) {
+  if (handle < 0 || handle >= (int)g_kernels.size() || g_kernels[handle] == nullptr) {
+    set_err(err, err_len, "bad kernel handle");
+    return ORT_INVALID_ARGUMENT;
+  }
+  HostKernel* hk = g_kernels[handle];
   std::vector<HostValue> vals(n_inputs);
   HostContext ctx;
   const int64_t* dp = dims;
@@ -285,25 +335,41 @@ int fake_ort_run(int lib, const char* name, int n_inputs, void* const* ptrs,
   ctx.stream = stream;
   auto* kctx = reinterpret_cast<OrtKernelContext*>(&ctx);
   int rc = 0;
-  if (use_v2 && op->CreateKernelV2 && op->KernelComputeV2) {
-    void* k = nullptr;
-    if (OrtStatus* s = op->CreateKernelV2(op, &kApi, nullptr, &k)) {
-      set_err(err, err_len, status_msg(s));
-      rc = status_code(s);
-      release_status(s);
-      return rc;
-    }
-    if (OrtStatus* s = op->KernelComputeV2(k, kctx)) {
+  if (hk->v2) {
+    if (OrtStatus* s = hk->op->KernelComputeV2(hk->kernel, kctx)) {
       set_err(err, err_len, status_msg(s));
       rc = status_code(s);
       release_status(s);
     }
-    op->KernelDestroy(k);
   } else {
-    void* k = op->CreateKernel(op, &kApi, nullptr);
-    op->KernelCompute(k, kctx);
-    op->KernelDestroy(k);
+    hk->op->KernelCompute(hk->kernel, kctx);
   }
+  return rc;
+}
+
+void fake_ort_kernel_destroy(int handle) {
+  if (handle < 0 || handle >= (int)g_kernels.size() || g_kernels[handle] == nullptr) return;
+  g_kernels[handle]->op->KernelDestroy(g_kernels[handle]->kernel);
+  delete g_kernels[handle];
+  g_kernels[handle] = nullptr;
+}
+
+// Run op `name` of library `lib` once with a kernel of its own (created and
+// destroyed around the call). ptrs[i] == NULL marks an omitted optional
+// input. dims holds the inputs' dims back to back (ranks[i] each); types[i]
+// is the ONNX element type. Returns 0 or the OrtErrorCode of the status the
+// op returned (message in err). use_v2 = 0 runs the void KernelCompute entry.
+int fake_ort_run(int lib, const char* name, int n_inputs, void* const* ptrs,
+                 const int64_t* dims, const int* ranks, const int* types, void* out,
+                 const int64_t* out_dims, int out_rank, void* stream, int use_v2, char* err,
+                 size_t err_len) {
+  const int h = fake_ort_kernel_create(lib, name, use_v2, err, err_len);
+  if (h < 0) {
+    return find_op(lib, name) ? ORT_FAIL : ORT_NOT_IMPLEMENTED;
+  }
+  const int rc = fake_ort_kernel_run(h, n_inputs, ptrs, dims, ranks, types, out, out_dims,
+                                     out_rank, stream, err, err_len);
+  fake_ort_kernel_destroy(h);
   return rc;
 }
 

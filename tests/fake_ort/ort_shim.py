@@ -49,6 +49,18 @@ def host():
             [ctypes.POINTER(ctypes.c_int)] * 5 + [ctypes.c_char_p, ctypes.c_size_t]
         h.fake_ort_fail_next.argtypes = [ctypes.c_char_p]
         h.fake_ort_live_allocations.restype = ctypes.c_int
+        h.fake_ort_kernel_create.restype = ctypes.c_int
+        h.fake_ort_kernel_create.argtypes = [ctypes.c_int, ctypes.c_char_p, ctypes.c_int,
+                                             ctypes.c_char_p, ctypes.c_size_t]
+        h.fake_ort_kernel_run.restype = ctypes.c_int
+        h.fake_ort_kernel_run.argtypes = [ctypes.c_int, ctypes.c_int,
+                                          ctypes.POINTER(ctypes.c_void_p),
+                                          ctypes.POINTER(ctypes.c_int64),
+                                          ctypes.POINTER(ctypes.c_int),
+                                          ctypes.POINTER(ctypes.c_int), ctypes.c_void_p,
+                                          ctypes.POINTER(ctypes.c_int64), ctypes.c_int,
+                                          ctypes.c_void_p, ctypes.c_char_p, ctypes.c_size_t]
+        h.fake_ort_kernel_destroy.argtypes = [ctypes.c_int]
         h.fake_ort_run.restype = ctypes.c_int
         h.fake_ort_run.argtypes = [ctypes.c_int, ctypes.c_char_p, ctypes.c_int,
                                    ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_int64),
@@ -138,7 +150,11 @@ def make_model(op_name: str, use_fused: bool, with_delta_bias: bool = False) -> 
 
 
 class InferenceSession:
-    """Runs a SingleOpModel through the registered library on one CUDA device."""
+    """Runs a SingleOpModel through the registered library on one CUDA device.
+
+    Like ONNX Runtime, a session creates the node's kernel once (through the
+    op's CreateKernelV2, or CreateKernel with use_v2=False) and runs that same
+    kernel on every run() until close(), which calls KernelDestroy."""
 
     def __init__(self, model: SingleOpModel, sess_options: SessionOptions, providers=None,
                  use_v2: bool = True):
@@ -147,6 +163,7 @@ class InferenceSession:
         providers = list(providers or ["CUDAExecutionProvider"])
         self.model = model
         self.lib = None
+        self.kernel = -1
         for lib in sess_options.libraries:
             for info in op_infos(lib):
                 if info.name == model.op_type and info.ep in providers:
@@ -154,38 +171,69 @@ class InferenceSession:
         if self.lib is None:
             raise OrtError(9, f"no kernel registered for {model.op_type} on {providers}")
         self.use_v2 = use_v2
+        err = ctypes.create_string_buffer(1024)
+        self.kernel = host().fake_ort_kernel_create(self.lib, model.op_type.encode(),
+                                                    1 if use_v2 else 0, err, len(err))
+        if self.kernel < 0:
+            raise OrtError(1, err.value.decode())
 
-    def run(self, output_names, feed: dict, stream=None):
+    def close(self):
+        if self.kernel >= 0:
+            host().fake_ort_kernel_destroy(self.kernel)
+            self.kernel = -1
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001 - interpreter shutdown
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def run_device(self, inputs, out, stream=None):
+        """Enqueue one run on device tensors (torch, in the model's input order;
+        None = an omitted optional input) writing `out`, on `stream` (default:
+        torch's current stream). Nothing is synchronised."""
         import torch
 
-        dev_inputs, ptrs, dims, ranks, types = [], [], [], [], []
-        for name in self.model.inputs:
-            a = feed.get(name)
-            if a is None:
+        ptrs, dims, ranks, types = [], [], [], []
+        for t in inputs:
+            if t is None:
                 ptrs.append(None)
                 ranks.append(0)
                 types.append(FLOAT)
                 continue
-            a = np.ascontiguousarray(a)
-            t = torch.from_numpy(a).cuda()
-            dev_inputs.append(t)
             ptrs.append(t.data_ptr())
-            dims.extend(a.shape)
-            ranks.append(a.ndim)
-            types.append(DOUBLE if a.dtype == np.float64 else FLOAT)
+            dims.extend(t.shape)
+            ranks.append(t.dim())
+            types.append(DOUBLE if t.dtype == torch.float64 else FLOAT)
+        st = stream or torch.cuda.current_stream()
+        err = ctypes.create_string_buffer(2048)
+        out_dims = (ctypes.c_int64 * out.dim())(*out.shape)
+        n = len(ptrs)
+        rc = host().fake_ort_kernel_run(
+            self.kernel, n, (ctypes.c_void_p * n)(*ptrs),
+            (ctypes.c_int64 * max(1, len(dims)))(*dims), (ctypes.c_int * n)(*ranks),
+            (ctypes.c_int * n)(*types), out.data_ptr(), out_dims, out.dim(), st.cuda_stream,
+            err, len(err))
+        if rc != 0:
+            raise OrtError(rc, err.value.decode())
+        return out
+
+    def run(self, output_names, feed: dict, stream=None):
+        import torch
+
+        dev = [None if feed.get(name) is None else
+               torch.from_numpy(np.ascontiguousarray(feed[name])).cuda()
+               for name in self.model.inputs]
         u = feed["u"]
         out = torch.empty(tuple(u.shape), dtype=torch.float32, device="cuda")
         out.fill_(float("nan"))
         st = stream or torch.cuda.current_stream()
-        err = ctypes.create_string_buffer(2048)
-        out_dims = (ctypes.c_int64 * 3)(*u.shape)
-        n = len(ptrs)
-        rc = host().fake_ort_run(
-            self.lib, self.model.op_type.encode(), n, (ctypes.c_void_p * n)(*ptrs),
-            (ctypes.c_int64 * max(1, len(dims)))(*dims), (ctypes.c_int * n)(*ranks),
-            (ctypes.c_int * n)(*types), out.data_ptr(), out_dims, 3, st.cuda_stream,
-            1 if self.use_v2 else 0, err, len(err))
-        if rc != 0:
-            raise OrtError(rc, err.value.decode())
+        self.run_device(dev, out, st)
         st.synchronize()
         return [out.cpu().numpy()]

@@ -10,12 +10,14 @@ fake_ort/ort_shim.py). Each case is checked against
   cross-backend agreement, with this backend in place of zig).
 """
 import numpy as np
+import torch
 import pytest
 
 import golden_cases as gc
 import mamba_onnx
 import scan_cases as sc
 from fake_ort import ort_shim
+from mamba_onnx import cuda
 from oracle import oracle
 
 pytestmark = pytest.mark.gpu
@@ -26,9 +28,9 @@ def _run_onnx(op_name, use_fused, feed, use_v2=True):
     opts = ort_shim.SessionOptions()
     mamba_onnx.register_custom_ops(opts, backend="cuda")
     model = ort_shim.make_model(op_name, use_fused, with_delta_bias="delta_bias" in feed)
-    sess = ort_shim.InferenceSession(model, opts, providers=["CUDAExecutionProvider"],
-                                     use_v2=use_v2)
-    return sess.run(None, feed)[0]
+    with ort_shim.InferenceSession(model, opts, providers=["CUDAExecutionProvider"],
+                                   use_v2=use_v2) as sess:
+        return sess.run(None, feed)[0]
 
 
 def _feed(u, delta, A, B, C, D, z):
@@ -130,7 +132,8 @@ def test_optional_delta_bias_input():
 
 
 def test_long_sequence_uses_workspace_and_releases_it():
-    """A 1x64x4096 shape takes the chunked path; its ORT scratch is freed."""
+    """A 1x64x4096 shape takes the chunked path; its ORT scratch is returned
+    when the kernel is destroyed (the session closes)."""
     u, delta, A, B, C, D, z, _ = sc.config_inputs(1, 64, 4096, False, seed=4,
                                                   exact_dt_per_element=True)
     before = ort_shim.live_allocations()
@@ -139,3 +142,69 @@ def test_long_sequence_uses_workspace_and_releases_it():
     ref = oracle.scan_f64("SelectiveScanExact", u, delta, A, B, C, D)
     assert np.linalg.norm(out - ref) / np.linalg.norm(ref) <= 1e-5
     np.testing.assert_allclose(out, ref, rtol=1e-4, atol=1e-4)
+
+
+def _dev_inputs(op, batch, dim, seqlen, seed):
+    fused = oracle.OPS[op][1]
+    arrs = sc.config_inputs(batch, dim, seqlen, fused, seed=seed,
+                            exact_dt_per_element=not fused)[:7]
+    return arrs, [None if a is None else torch.from_numpy(np.ascontiguousarray(a)).cuda()
+                  for a in arrs]
+
+
+def test_one_kernel_on_two_streams_keeps_separate_scratch():
+    """ONNX Runtime keeps one kernel object per node and may run it on several
+    streams at once (multi-stream execution, concurrent sessions runs). The
+    chunked path's scratch must then not be shared: two shapes that split their
+    sequences run interleaved on two streams, with nothing ordering one stream
+    against the other, three times each through one kernel; every output
+    matches the oracle, and the kernel holds one buffer per stream until
+    KernelDestroy returns them."""
+    op = "SelectiveScanExact"
+    opts = ort_shim.SessionOptions()
+    mamba_onnx.register_custom_ops(opts, backend="cuda")
+    before = ort_shim.live_allocations()
+    (a_np, a_dev), (b_np, b_dev) = (_dev_inputs(op, 1, 64, 4096, 31),
+                                    _dev_inputs(op, 1, 96, 3000, 32))
+    assert cuda.workspace_size(op, 1, 64, 4096) > 0 and cuda.workspace_size(op, 1, 96, 3000) > 0
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+    with ort_shim.InferenceSession(ort_shim.make_model(op, False), opts) as sess:
+        outs = []
+        for _ in range(3):
+            oa = torch.full_like(a_dev[0], float("nan"))
+            ob = torch.full_like(b_dev[0], float("nan"))
+            sess.run_device(a_dev[:6], oa, s1)
+            sess.run_device(b_dev[:6], ob, s2)
+            outs.append((oa, ob))
+        torch.cuda.synchronize()
+        assert ort_shim.live_allocations() == before + 2
+        for arrs, got in [(a_np, [o[0] for o in outs]), (b_np, [o[1] for o in outs])]:
+            ref = oracle.scan_f64(op, *arrs[:6])
+            for g in got:
+                g = g.cpu().numpy()
+                assert np.linalg.norm(g - ref) / np.linalg.norm(ref) <= 1e-5
+                np.testing.assert_allclose(g, ref, rtol=1e-4, atol=1e-4)
+    assert ort_shim.live_allocations() == before
+
+
+def test_kernel_scratch_grows_for_a_larger_shape():
+    """A larger shape on the same stream gets a larger buffer; the outgrown one
+    stays allocated (work already enqueued may read it) until KernelDestroy."""
+    op = "SelectiveScanFused"
+    opts = ort_shim.SessionOptions()
+    mamba_onnx.register_custom_ops(opts, backend="cuda")
+    before = ort_shim.live_allocations()
+    small_np, small = _dev_inputs(op, 1, 32, 1024, 41)
+    big_np, big = _dev_inputs(op, 1, 256, 4096, 42)
+    assert 0 < cuda.workspace_size(op, 1, 32, 1024) < cuda.workspace_size(op, 1, 256, 4096)
+    with ort_shim.InferenceSession(ort_shim.make_model(op, True), opts) as sess:
+        o_small, o_big = torch.empty_like(small[0]), torch.empty_like(big[0])
+        sess.run_device(small, o_small)
+        sess.run_device(big, o_big)
+        sess.run_device(small, o_small)
+        torch.cuda.synchronize()
+        assert ort_shim.live_allocations() == before + 2
+        for arrs, got in [(small_np, o_small), (big_np, o_big)]:
+            ref = oracle.scan_f64(op, *arrs)
+            np.testing.assert_allclose(got.cpu().numpy(), ref, rtol=1e-3, atol=1e-3)
+    assert ort_shim.live_allocations() == before

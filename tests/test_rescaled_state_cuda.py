@@ -1,12 +1,19 @@
 """GPU: inputs that stress the linear ops' rescaled state.
 
 SelectiveScan and SelectiveScanFused run their recurrence on g = h / w with
-w = delta*u (|w| held at 1e-12 or above), so zero, tiny, denormal,
-sign-flipping or widely ranging delta*u must leave the result unchanged. Each
-case checks the output and the final state of all four ops against the
-oracle's float64 restatement at the reference tests' tolerance
-(rtol = atol = 1e-4, tests/test_ops.py:171), through the single-pass TMA path
-(with a partial last tile), the chunked path and the plain-load path.
+w = delta*u, falling back to h itself for any 16-step tile where |w| is tiny
+against |h|, so zero, tiny, denormal, sign-flipping or widely ranging delta*u
+must leave the result unchanged. Each case checks the output and the final
+state of all four ops against the oracle's float64 restatement at the
+reference tests' tolerance (rtol = atol = 1e-4, tests/test_ops.py:171),
+through the single-pass TMA path (with a partial last tile), the chunked path
+and the plain-load path.
+
+The growing-state cases run the reference tests' large_delta regime
+(tests/test_ops.py:219-236: delta = 2, so |1 + delta*A| reaches 2 and the
+state grows about 2^L) over 128 and 256 steps with u = 0 at some steps: |h|
+reaches 1e27-1e37, where g = h / w would overflow at every u = 0 step, while
+the reference's float32 h stays finite.
 """
 import zlib
 
@@ -74,3 +81,79 @@ def test_stressed_inputs_match_oracle(op, case, shape):
     np.testing.assert_allclose(got, ref, rtol=1e-4, atol=1e-4 * scale)
     np.testing.assert_allclose(h_last.cpu().numpy().reshape(-1, 16), h_ref, rtol=1e-4,
                                atol=1e-4 * scale)
+
+
+def _zero_steps(u):
+    u = u.copy()
+    L = u.shape[2]
+    u[..., ::9] = 0.0          # every ninth step, the first included
+    u[..., 15:18] = 0.0        # across a tile boundary
+    u[..., L - 1] = 0.0        # the last step
+    return u
+
+
+def _growth_inputs(op, B, D, L):
+    """large_delta inputs (seed 99 recipe) with zero-u steps. Over 256 steps
+    the reference's A range is narrowed so float32 keeps the state finite
+    (max |1 + delta*A| 1.3 for SelectiveScan, 1.5 for SelectiveScanFused).
+    SelectiveScanFused gets delta = softplus^-1 of U[1.8, 2.0] per element."""
+    u, delta, A, Bm, C, Dv, _ = sc.edge_case_inputs("large_delta", B=B, D=D, L=L)
+    fused = oracle.OPS[op][1]
+    if L > 128:
+        amp = 0.75 if fused else 0.65
+        A = (-np.random.default_rng(0).random(A.shape) * amp - 0.5).astype(np.float32)
+    z = None
+    if fused:
+        rng = np.random.default_rng(2)
+        delta = np.log(np.expm1(rng.uniform(1.8, 2.0, delta.shape))).astype(np.float32)
+        z = rng.standard_normal(u.shape).astype(np.float32)
+    return _zero_steps(u), delta, A, Bm, C, Dv, z
+
+
+def _output_scale(u, delta, A, Bm, C, Dv, z):
+    """Float64 (sum_n |C_n h_n| + |D u|) * |silu(z)| per output: the size of
+    the terms each output sums, against which its rounding error is judged."""
+    d = delta.astype(np.float64)
+    if z is not None:
+        d = np.logaddexp(0.0, d)
+    B, D, L = u.shape
+    scale = np.empty((B, D, L))
+    for b in range(B):
+        h = np.zeros((D, 16))
+        for t in range(L):
+            h = (1.0 + d[b, :, t, None] * A) * h + (d[b, :, t] * u[b, :, t])[:, None] * Bm[b, t]
+            scale[b, :, t] = np.abs(h * C[b, t]).sum(1) + np.abs(Dv * u[b, :, t])
+    if z is not None:
+        zz = z.astype(np.float64)
+        scale *= np.abs(zz / (1.0 + np.exp(-zz)))
+    return scale
+
+
+# (batch, dim, seqlen, chunked): chunked splits the sequence (aggregate, carry
+# and emit passes); 126 and 254 steps take the plain-load path
+GROWTH_SHAPES = [(1, 64, 128, True), (1, 64, 128, False), (2, 40, 126, True),
+                 (1, 64, 256, True), (1, 64, 256, False), (2, 40, 254, True)]
+
+
+@pytest.mark.parametrize("shape", GROWTH_SHAPES,
+                         ids=[f"{b}x{d}x{l}{'' if c else '-single'}" for b, d, l, c in GROWTH_SHAPES])
+@pytest.mark.parametrize("op", ["SelectiveScan", "SelectiveScanFused"])
+def test_growing_state_with_zero_inputs_stays_finite(op, shape):
+    """The linear ops stay finite and match the float64 oracle where the
+    reference's float32 state reaches 1e27-1e37 and u = 0 at some steps
+    (rtol 1e-4 on each output's own scale)."""
+    B, D, L, chunked = shape
+    u, delta, A, Bm, C, Dv, z = _growth_inputs(op, B, D, L)
+    h_last = torch.empty(B, D, 16, device="cuda")
+    out = cuda.selective_scan(op, _dev(u), _dev(delta), _dev(A), _dev(Bm), _dev(C), _dev(Dv),
+                              _dev(z), h_last=h_last, chunked=chunked)
+    got = out.cpu().numpy().astype(np.float64)
+    ref, h_ref = oracle.scan_f64(op, u, delta, A, Bm, C, Dv, z, return_state=True)
+    assert np.abs(ref).max() > 1e26  # beyond where g = h / (1e-12) overflowed
+    assert np.isfinite(got).all()
+    scale = _output_scale(u, delta, A, Bm, C, Dv, z)
+    err = np.abs(got - ref) / np.maximum(scale, 1e-30)
+    assert err.max() <= 1e-4, f"max scaled error {err.max():.3e}"
+    hl = h_last.cpu().numpy().reshape(-1, 16).astype(np.float64)
+    assert np.isfinite(hl).all()
+    np.testing.assert_allclose(hl, h_ref, rtol=1e-4, atol=1e-4 * np.abs(h_ref).max())

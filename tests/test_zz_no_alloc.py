@@ -65,7 +65,11 @@ def test_static_workspace_matches_caller_workspace(op, batch, dim, seqlen):
 
 
 def test_static_workspace_after_a_different_shape():
-    """A call does not depend on what the previous call left in the array."""
+    """A call does not depend on what the previous call left in the array:
+    two shapes that both need scratch, back to back, each match the
+    caller-workspace path."""
+    assert cuda.workspace_size("SelectiveScanExact", 1, 1024, 8192) > 0
+    assert cuda.workspace_size("SelectiveScan", 1, 512, 3000) > 0
     stream = torch.cuda.current_stream().cuda_stream
     first = _inputs("SelectiveScanExact", 1, 1024, 8192, seed=5)
     out1 = torch.empty_like(first[0])
@@ -74,6 +78,8 @@ def test_static_workspace_after_a_different_shape():
     out2 = torch.empty_like(second[0])
     assert cuda.launch_static_workspace(0, _args(*second, out2), stream) == 0
     torch.cuda.synchronize()
+    torch.testing.assert_close(out1, cuda.selective_scan("SelectiveScanExact", *first[:6]),
+                               rtol=RTOL, atol=ATOL)
     torch.testing.assert_close(out2, cuda.selective_scan("SelectiveScan", *second[:6]),
                                rtol=RTOL, atol=ATOL)
 
@@ -99,7 +105,9 @@ def test_static_workspace_rejects_shapes_that_need_more():
     if not big:
         pytest.skip("no shape needs more than the built-in 8 MiB on this GPU")
     op, batch, dim, seqlen = big[0]
-    fake = cuda.ScanArgs(0x1000, 0x2000, 0x3000, 0x4000, 0x5000, 0x6000, 0x8000, None, None,
-                         0x7000, None, batch, dim, seqlen, 16)
-    assert cuda.launch_static_workspace(cuda.OPS[op], fake, None) == 3
+    # NULL tensors: were the size check ever to pass such a shape, the scan's
+    # own NULL check would still refuse it before any launch
+    args = cuda.ScanArgs(None, None, None, None, None, None, None, None, None, None, None,
+                         batch, dim, seqlen, 16)
+    assert cuda.launch_static_workspace(cuda.OPS[op], args, None) == 3
     assert "built-in workspace" in cuda.library().mamba_scan_last_error().decode()
