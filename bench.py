@@ -4,19 +4,22 @@
 
 One step = one selective scan over the whole per-GPU batch (inputs resident in
 HBM). With N GPUs (one process per GPU, launched by torch.distributed.run)
-each rank scans its own batch-8 shard: the op shards by batch with no
-exchange, so the scaling is weak and no collective touches the data path.
-Rank 0 prints one JSON line.
+each rank scans its own batch-8 shard of a batch-8N job: the op shards by
+batch with no exchange, so the scaling is weak. After the timed steps the
+output shards are gathered to rank 0 through NCCL (the op's one collective),
+timed on its own (gather_ms). Rank 0 prints one JSON line.
 
 value     — scan elements (batch*d_inner*seqlen*d_state, all ranks) per second,
             timed with CUDA events over K steps, max over ranks.
-e2e       — the same metric end to end through the public API with host
-            buffers: pinned host inputs -> H2D -> scan -> D2H of the output,
-            pipelined per batch entry on two streams.
+e2e       — the same metric end to end through the ONNX Runtime custom-op
+            entry (RegisterCustomOps -> CreateKernelV2 -> KernelComputeV2,
+            driven by the CUDA-EP host of tests/fake_ort, ORT itself not being
+            installed) with host buffers: pinned host inputs -> H2D -> op ->
+            D2H of the output, pipelined per batch entry on two streams.
 roofline  — the scan kernel's algorithmic HBM bytes per launch / its launch
             duration, against the measured copy bandwidth.
 cpu_baseline — the reference's own C++ plugin (oracle/_ref, OpenMP, all host
-            threads) on a sample of the same workload.
+            threads) on the same workload (all 8 batch entries).
 --impl reference runs that reference plugin alone, as the reference arm.
 
     python bench.py --workload mamba130m [--gpus N] [--steps K] [--warmup W]
@@ -170,32 +173,42 @@ def device_inputs(torch, device, seed):
 
 # ---------------------------------------------------------------- CPU baseline
 
-def reference_sample(n_threads, reps, budget_s=60.0):
-    """The reference C++ plugin on batch entry 0 of the workload (host arrays).
-
-    Runs up to `reps` timed calls, stopping early once `budget_s` seconds of
-    timed work have accumulated."""
-    from oracle import oracle
-
+def reference_inputs(entries):
+    """Host copies of `entries` batch entries of the workload, drawn with the
+    benchmark distributions from a seeded Philox stream."""
     g = np.random.Generator(np.random.Philox(SEED))
     D, L = DIM, SEQLEN
-    u = g.standard_normal((1, D, L), dtype=np.float32)
-    z = g.standard_normal((1, D, L), dtype=np.float32)
-    Bm = g.standard_normal((1, L, NSTATE), dtype=np.float32)
-    Cm = g.standard_normal((1, L, NSTATE), dtype=np.float32)
+    u = g.standard_normal((entries, D, L), dtype=np.float32)
+    z = g.standard_normal((entries, D, L), dtype=np.float32)
+    Bm = g.standard_normal((entries, L, NSTATE), dtype=np.float32)
+    Cm = g.standard_normal((entries, L, NSTATE), dtype=np.float32)
     dt = np.exp(g.uniform(np.log(1e-3), np.log(1e-1), D)).astype(np.float32)
-    delta = (g.standard_normal((1, D, L), dtype=np.float32) * np.float32(0.5)
+    delta = (g.standard_normal((entries, D, L), dtype=np.float32) * np.float32(0.5)
              + np.log(np.expm1(dt.astype(np.float64))).astype(np.float32)[None, :, None])
     A = -np.tile(np.arange(1, NSTATE + 1, dtype=np.float32), (D, 1))
     Dv = np.ones(D, np.float32)
-    out = np.empty((1, D, L), np.float32)
+    return u, delta, A, Bm, Cm, Dv, z
+
+
+def reference_timer(n_threads):
+    """(fn, kind, threads): one call of the reference's C++ plugin (oracle/_ref,
+    OpenMP) over the whole per-GPU workload (batch 8 x 5120 x 2048), or of the
+    scalar port when the plugin was not built."""
+    from oracle import oracle
+
+    u, delta, A, Bm, Cm, Dv, z = reference_inputs(BATCH)
+    out = np.empty_like(u)
     if oracle.ref_available():
-        kind = "reference"
-        fn = lambda: oracle.ref_run(OP, u, delta, A, Bm, Cm, Dv, z, n_threads=n_threads,  # noqa
-                                    out=out)
-    else:
-        kind, n_threads = "port", 1
-        fn = lambda: oracle.scan_f32ref(OP, u, delta, A, Bm, Cm, Dv, z)  # noqa: E731
+        return (lambda: oracle.ref_run(OP, u, delta, A, Bm, Cm, Dv, z, n_threads=n_threads,
+                                       out=out)), "reference", n_threads
+    return (lambda: oracle.scan_f32ref(OP, u, delta, A, Bm, Cm, Dv, z)), "port", 1
+
+
+def reference_sample(n_threads, reps, budget_s=30.0):
+    """The reference C++ plugin on the full per-GPU workload (host arrays):
+    up to `reps` timed calls after one warm-up, stopping once `budget_s`
+    seconds of timed work have accumulated."""
+    fn, kind, n_threads = reference_timer(n_threads)
     fn()  # warm-up (page-in, thread pool)
     times = []
     for _ in range(reps):
@@ -204,33 +217,40 @@ def reference_sample(n_threads, reps, budget_s=60.0):
         times.append(time.perf_counter() - t0)
         if sum(times) > budget_s:
             break
-    reps = len(times)
-    elems = D * L * NSTATE
+    elems = BATCH * DIM * SEQLEN * NSTATE
     return {"value": elems / statistics.median(times), "unit": UNIT, "cores": n_threads,
             "kind": kind,
-            "sample": f"batch entry 0 of the workload (1x{D}x{L}), median of {reps} runs "
-                      f"after 1 warm-up, {n_threads} OpenMP threads"}
+            "sample": f"the full workload ({BATCH}x{DIM}x{SEQLEN}) per call, median of "
+                      f"{len(times)} calls after 1 warm-up, {n_threads} OpenMP threads"}
 
 
 def run_reference_arm(args, rank):
+    """The reference's C++ plugin on the host cores, one call over the whole
+    per-GPU workload per step: W warm-up calls, then K timed calls."""
     if rank != 0:
         return
     from oracle import oracle
 
-    threads = oracle.host_threads()
-    per_step = reference_sample(threads, reps=max(1, args.steps))
+    fn, kind, threads = reference_timer(oracle.host_threads())
+    for _ in range(args.warmup):
+        fn()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        fn()
+    sec = (time.perf_counter() - t0) / args.steps
+    value = BATCH * DIM * SEQLEN * NSTATE / sec
     line = {
-        "impl": "reference", "metric": METRIC, "value": per_step["value"], "unit": UNIT,
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1e3 * DIM * SEQLEN * NSTATE / per_step["value"],
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic",
+        "ms_per_step": 1e3 * sec, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": WORKLOAD, "op": OP, "batch_per_gpu": BATCH, "d_inner": DIM,
                    "seqlen": SEQLEN, "d_state": NSTATE,
-                   "step": "one reference plugin call on batch entry 0 (1/8 of the per-GPU batch)"},
-        "cpu_baseline": per_step,
-        "e2e": {"value": per_step["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
-                "d2h_bytes_per_step": 0},
+                   "step": "one reference plugin call on the whole batch 8 x 5120 x 2048"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": kind,
+                         "sample": f"the full workload per step, mean of {args.steps} calls "
+                                   f"after {args.warmup} warm-up calls"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
@@ -240,7 +260,9 @@ def run_reference_arm(args, rank):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--steps", type=int, default=None,
+                    help="timed steps (default 2000; 20 for --impl reference, whose step is "
+                         "one ~0.1-0.2 s host call)")
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
     ap.add_argument("--e2e-steps", type=int, default=10)
@@ -257,6 +279,8 @@ def main():
                          "GEMM on random [M,K] x [N,K] operands; nothing timed")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
+    if args.steps is None:
+        args.steps = 20 if args.impl == "reference" else 2000
     if args.workload == "mamba130m":
         return run_model(args)
     if args.workload == "mamba130m-decode":
@@ -340,8 +364,13 @@ def main():
     elems_per_step = BATCH * DIM * SEQLEN * NSTATE
     value = world * elems_per_step / (ms_per_step * 1e-3)
 
-    # ---- end to end through the public API, host buffers (pinned), per-entry pipeline
-    e2e = end_to_end(torch, cuda, device, args, world)
+    # ---- the op's one collective: every rank's output shard to rank 0 (NCCL)
+    gather = None
+    if world > 1:
+        gather = gather_to_rank0(torch, dist, out, world, rank, device, stream)
+
+    # ---- end to end through the custom-op entry, host buffers (pinned), per-entry pipeline
+    e2e = end_to_end(torch, device, args, world)
 
     if rank == 0:
         hbm_peak, peak_kind = measured_peaks()
@@ -358,8 +387,13 @@ def main():
             "data": "synthetic",
             "config": {"workload": WORKLOAD, "op": OP, "batch_per_gpu": BATCH,
                        "global_batch": BATCH * world, "d_inner": DIM, "seqlen": SEQLEN,
-                       "d_state": NSTATE, "parallelism": f"batch-sharded x{world}, no collective",
+                       "d_state": NSTATE,
+                       "parallelism": (f"batch-sharded x{world}; the output gathered to rank 0 "
+                                       "by NCCL after the timed steps (gather_ms)"
+                                       if world > 1 else "one GPU"),
                        "l2": "inputs 1.34 GB per GPU, larger than L2; no flush"},
+            "nccl_ranks": world if world > 1 else None,
+            "gather": gather,
             "e2e": e2e,
             "gpu_launches": launches_per_step * args.steps,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
@@ -377,8 +411,56 @@ def main():
         dist.destroy_process_group()
 
 
-def end_to_end(torch, cuda, device, args, world):
-    """Host->device, scan, device->host per step, through mamba_onnx.cuda.selective_scan."""
+def gather_to_rank0(torch, dist, out, world, rank, device, stream, reps=5):
+    """Gather every rank's [8, 5120, 2048] output shard into a preallocated
+    [8N, 5120, 2048] tensor on rank 0 (torch.distributed.gather over NCCL,
+    mamba_onnx.distributed.gather_output); one warm-up gather, then `reps`
+    timed ones, CUDA events, max over ranks. The result is checked against
+    rank 0's own shard and one remote shard's checksum."""
+    from mamba_onnx.distributed import gather_output, shard_plan
+
+    plan = shard_plan(BATCH * world, DIM, world, rank)
+    full = torch.empty(BATCH * world, DIM, SEQLEN, device=device) if rank == 0 else None
+    gather_output(out, plan, out=full)
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        gather_output(out, plan, out=full)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / reps], device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    # rank 1's checksum against what landed in its slice on rank 0
+    s1 = torch.tensor([float(out.double().sum().item())], device=device, dtype=torch.float64)
+    sums = [torch.zeros_like(s1) for _ in range(world)]
+    dist.all_gather(sums, s1)
+    ok = None
+    if rank == 0:
+        ok = bool(torch.equal(full[:BATCH], out)) and all(
+            float(full[r * BATCH:(r + 1) * BATCH].double().sum().item()) == float(sums[r].item())
+            for r in range(world))
+    moved = (world - 1) * out.numel() * 4
+    del full
+    return {"gather_ms": ms, "bytes_to_rank0": moved, "GBps_into_rank0": moved / (ms * 1e-3) / 1e9,
+            "reps": reps, "collective": "torch.distributed.gather (NCCL) into a preallocated "
+                                        "rank-0 tensor", "checked": ok}
+
+
+def end_to_end(torch, device, args, world):
+    """Host -> device, the op, device -> host per step, through the ONNX Runtime
+    custom-op entry of libmamba_ops_cuda.so (RegisterCustomOps, CreateKernelV2
+    once, KernelComputeV2 per batch entry) on the CUDA-EP host of tests/fake_ort."""
+    sys.path.insert(0, str(ROOT / "tests"))
+    import mamba_onnx
+    from fake_ort import ort_shim
+
+    opts = ort_shim.SessionOptions()
+    mamba_onnx.register_custom_ops(opts, backend="cuda")
+    sess = ort_shim.InferenceSession(ort_shim.make_model(OP, True), opts,
+                                     providers=["CUDAExecutionProvider"])
     B, D, L = BATCH, DIM, SEQLEN
     gen = torch.Generator().manual_seed(7)
     host = {
@@ -408,9 +490,10 @@ def end_to_end(torch, cuda, device, args, world):
             with torch.cuda.stream(s):
                 for k in ("u", "delta", "z", "B", "C"):
                     dev[k][b].copy_(host[k][b], non_blocking=True)
-                cuda.selective_scan(OP, dev["u"][b:b + 1], dev["delta"][b:b + 1], dev["A"],
-                                    dev["B"][b:b + 1], dev["C"][b:b + 1], dev["D"],
-                                    dev["z"][b:b + 1], out=dev_out[b:b + 1], stream=s)
+                # inputs in the op's order u, delta, A, B, C, D, z (cc:167-186)
+                sess.run_device([dev["u"][b:b + 1], dev["delta"][b:b + 1], dev["A"],
+                                 dev["B"][b:b + 1], dev["C"][b:b + 1], dev["D"],
+                                 dev["z"][b:b + 1]], dev_out[b:b + 1], stream=s)
                 host_out[b].copy_(dev_out[b], non_blocking=True)
         for s in streams:
             main.wait_stream(s)
@@ -426,6 +509,7 @@ def end_to_end(torch, cuda, device, args, world):
     e1.record(main)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / n
+    sess.close()
     if world > 1:
         import torch.distributed as dist
 
@@ -436,7 +520,10 @@ def end_to_end(torch, cuda, device, args, world):
     d2h = host_out.numel() * 4
     return {"value": world * B * D * L * NSTATE / (ms * 1e-3), "unit": UNIT,
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": ms,
-            "steps": n, "pipeline": "per batch entry on 2 streams, pinned host buffers"}
+            "steps": n, "path": "ONNX Runtime custom-op entry: RegisterCustomOps -> "
+                                "CreateKernelV2 -> KernelComputeV2 per batch entry "
+                                "(tests/fake_ort CUDA-EP host)",
+            "pipeline": "per batch entry on 2 streams, pinned host buffers"}
 
 
 # ---------------------------------------------------------------- Mamba-130m forward
@@ -721,7 +808,8 @@ def run_scan_b64(args):
             print(json.dumps({"impl": "reference", "metric": METRIC, "value": cpu["value"],
                               "unit": UNIT, "n_gpus": args.gpus, "cpu_baseline": cpu,
                               "config": {"workload": B64_WORKLOAD,
-                                         "step": "one reference plugin call on 1x5120x2048"},
+                                         "step": "one reference plugin call on 8x5120x2048 "
+                                                 "(one GPU's shard at 8 GPUs)"},
                               "e2e": {"value": cpu["value"], "unit": UNIT,
                                       "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
         return

@@ -40,6 +40,25 @@ typedef enum mamba_scan_variant {
   MAMBA_SCAN_FUSED_EXACT = 3  /* "SelectiveScanFusedExact": both                         */
 } mamba_scan_variant;
 
+/*
+ * Exact variants only: how exp is formed, OR'ed into the variant argument of
+ * mamba_scan_launch, mamba_scan_launch_static_workspace and
+ * mamba_scan_workspace_size. No flag: abar = exp(delta*A) and the chunk decay
+ * on the SFU (ex2.approx, relative error ~2 ulp), softplus/SiLU with CUDA's
+ * expf/log1pf.
+ *   MAMBA_SCAN_EXP_IEEE       CUDA's expf for abar and the chunk decay too.
+ *   MAMBA_SCAN_EXP_REFERENCE  the reference C++ backend's own exp (its
+ *     published degree-5 Taylor polynomial times 2^n, selective_scan.cc:33-69;
+ *     relative error up to ~8.6e-5) for abar, softplus and SiLU, so that the
+ *     output follows that backend's numbers (normwise within ~1e-6 of them)
+ *     rather than the exact function (~3e-4 from float64 at the benchmark
+ *     distributions). It also keeps that exp's one defect: -inf for
+ *     arguments below about -88.03.
+ * At most one flag; a flag on a non-exact variant is MAMBA_SCAN_ERR_INVALID_ARGUMENT.
+ */
+#define MAMBA_SCAN_EXP_IEEE 0x100
+#define MAMBA_SCAN_EXP_REFERENCE 0x200
+
 typedef enum mamba_scan_status {
   MAMBA_SCAN_OK = 0,
   MAMBA_SCAN_ERR_INVALID_ARGUMENT = 1, /* null pointer, bad variant, negative size   */

@@ -99,17 +99,35 @@ Plan make_plan(int64_t batch, int64_t dim, int64_t seqlen, int sms, int slots) {
   return pl;
 }
 
-// Resident emit CTAs per SM for a variant (cached per device).
-int emit_slots(int device, int variant, bool tma) {
-  static std::atomic<int> cache[64][4][2];
-  if (device < 0 || device >= 64 || variant < 0 || variant > 3) return 8;
-  int v = cache[device][variant][tma ? 1 : 0].load(std::memory_order_relaxed);
+// Resident emit CTAs per SM for a variant and exp mode (cached per device).
+int emit_slots(int device, int variant, int exp_mode, bool tma) {
+  static std::atomic<int> cache[64][4][3][2];
+  if (device < 0 || device >= 64 || variant < 0 || variant > 3 || exp_mode < 0 || exp_mode > 2)
+    return 8;
+  auto& slot = cache[device][variant][exp_mode][tma ? 1 : 0];
+  int v = slot.load(std::memory_order_relaxed);
   if (v > 0) return v;
-  if (mamba_scan::max_blocks_per_sm(variant, mamba_scan::kLaunchEmit, tma, &v) != cudaSuccess ||
+  if (mamba_scan::max_blocks_per_sm(variant, exp_mode, mamba_scan::kLaunchEmit, tma, &v) !=
+          cudaSuccess ||
       v <= 0)
     v = 8;
-  cache[device][variant][tma ? 1 : 0].store(v, std::memory_order_relaxed);
+  slot.store(v, std::memory_order_relaxed);
   return v;
+}
+
+// Splits a variant argument into the variant (0..3) and the exp mode of its
+// MAMBA_SCAN_EXP_* flag (0 none, 1 IEEE, 2 reference); false if malformed.
+bool decode_variant(int code, int* variant, int* exp_mode) {
+  const int v = code & 0xff, flags = code & ~0xff;
+  if (v < 0 || v > 3) return false;
+  int e = 0;
+  if (flags == MAMBA_SCAN_EXP_IEEE) e = 1;
+  else if (flags == MAMBA_SCAN_EXP_REFERENCE) e = 2;
+  else if (flags != 0) return false;
+  if (e != 0 && v != MAMBA_SCAN_EXACT && v != MAMBA_SCAN_FUSED_EXACT) return false;
+  *variant = v;
+  *exp_mode = e;
+  return true;
 }
 
 size_t workspace_bytes_for(const Plan& pl) {
@@ -175,22 +193,27 @@ int set_last_error(int status, const std::string& msg) { return fail(status, msg
 
 extern "C" {
 
-size_t mamba_scan_workspace_size(int variant, int64_t batch, int64_t dim, int64_t seqlen,
+size_t mamba_scan_workspace_size(int variant_code, int64_t batch, int64_t dim, int64_t seqlen,
                                  int64_t dstate) {
-  if (variant < 0 || variant > 3 || batch <= 0 || dim <= 0 || seqlen <= 0 || dstate != 16)
+  int variant = 0, exp_mode = 0;
+  if (!decode_variant(variant_code, &variant, &exp_mode) || batch <= 0 || dim <= 0 ||
+      seqlen <= 0 || dstate != 16)
     return 0;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
   return workspace_bytes_for(
-      make_plan(batch, dim, seqlen, sm_count(dev), emit_slots(dev, variant, true)));
+      make_plan(batch, dim, seqlen, sm_count(dev), emit_slots(dev, variant, exp_mode, true)));
 }
 
-int mamba_scan_launch(int variant, const mamba_scan_args* a, void* workspace,
+int mamba_scan_launch(int variant_code, const mamba_scan_args* a, void* workspace,
                       size_t workspace_bytes, void* stream) {
   t_last_error.clear();
   if (a == nullptr) return fail(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "args is NULL");
-  if (variant < 0 || variant > 3)
-    return fail(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "variant must be 0..3");
+  int variant = 0, exp_mode = 0;
+  if (!decode_variant(variant_code, &variant, &exp_mode))
+    return fail(MAMBA_SCAN_ERR_INVALID_ARGUMENT,
+                "variant must be 0..3, with at most one MAMBA_SCAN_EXP_* flag (exact variants "
+                "only)");
   if (a->batch < 0 || a->dim < 0 || a->seqlen < 0 || a->dstate < 0)
     return fail(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "negative dimension");
   // selective_scan.cc:228-230 accepts only dstate == 16.
@@ -284,7 +307,7 @@ int mamba_scan_launch(int variant, const mamba_scan_args* a, void* workspace,
   }
 
   // (planned with the TMA kernel's occupancy, as mamba_scan_workspace_size does)
-  Plan pl = make_plan(B, D, L, sm_count(dev), emit_slots(dev, variant, true));
+  Plan pl = make_plan(B, D, L, sm_count(dev), emit_slots(dev, variant, exp_mode, true));
   const size_t need = workspace_bytes_for(pl);
   if (need > 0) {
     if (workspace == nullptr) {
@@ -310,13 +333,14 @@ int mamba_scan_launch(int variant, const mamba_scan_args* a, void* workspace,
   // alongside the aggregate pass; its chunk CTAs wait for the carry kernel.
   const bool split = pl.n_tail > 0 && pl.n_chunks > 1;
   if (split) {
-    e = mamba_scan::launch_scan_kernel(variant, mamba_scan::kLaunchAggregate, tma, p, maps,
-                                       (unsigned)(pl.n_tail * (pl.n_chunks - 1)), st, false);
+    e = mamba_scan::launch_scan_kernel(variant, exp_mode, mamba_scan::kLaunchAggregate, tma, p,
+                                       maps, (unsigned)(pl.n_tail * (pl.n_chunks - 1)), st,
+                                       false);
     if (e != cudaSuccess) return fail(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
     e = mamba_scan::launch_carry_kernel(p, st);
     if (e != cudaSuccess) return fail(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
   }
-  e = mamba_scan::launch_scan_kernel(variant, mamba_scan::kLaunchEmit, tma, p, maps,
+  e = mamba_scan::launch_scan_kernel(variant, exp_mode, mamba_scan::kLaunchEmit, tma, p, maps,
                                      (unsigned)(pl.n_full + pl.n_tail * pl.n_chunks), st, split);
   if (e != cudaSuccess) return fail(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
   return MAMBA_SCAN_OK;

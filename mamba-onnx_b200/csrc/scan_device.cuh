@@ -19,6 +19,16 @@ constexpr int kCarryThreads = 256;  // threads per CTA of the carry kernel
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // a tile wait gives up after 2 s
 
 enum Variant { kLinear = 0, kExact = 1, kFused = 2, kFusedExact = 3 };
+
+// How the Exact variants form exp (abar = exp(delta*A), the chunk decay, and
+// in reference mode the exps inside softplus and SiLU):
+//   kExpSfu       2^(x*log2 e) on the SFU (ex2.approx), softplus/SiLU with
+//                 CUDA's expf/log1pf;
+//   kExpIeee      CUDA's expf everywhere;
+//   kExpReference the reference C++ backend's own exp, its published Taylor-5
+//                 plus 2^n method, in softplus and SiLU too, so the output
+//                 follows that backend's (float64-inexact) numbers.
+enum ExpMode { kExpSfu = 0, kExpIeee = 1, kExpReference = 2 };
 enum Mode { kEmit = 0, kAggregate = 1 };
 
 template <int V> struct VariantTraits {
@@ -45,6 +55,12 @@ __device__ __forceinline__ void fence_mbarrier_init() {
 // async-proxy (TMA) accesses.
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Orders this thread's async-proxy (TMA) accesses, in every state space,
+// against its later generic-proxy accesses.
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async;" ::: "memory");
 }
 
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
@@ -189,6 +205,32 @@ __device__ __forceinline__ float rcp_approx(float x) {
   return y;
 }
 
+// exp(x) as the reference C++ backend computes it (selective_scan.cc:33-69,
+// method published in docs/optimization_notes.md:60-100): x clamped to
+// +-88.3762626647949, n = floor(x * 1.44269504089), f = x - n*ln2 in [0, ln2),
+// e^f by the degree-5 Taylor polynomial 1 + f + f^2/2 + ... + f^5/120 in Horner
+// form with FMAs, times 2^n formed as the bit pattern (n + 127) << 23. Every
+// step is a correctly rounded fp32 operation, so the result equals the
+// backend's bit for bit (denormal inputs aside: the backend runs with FTZ/DAZ).
+// For n = -128 (x below about -88.03) that pattern is the one of -inf, and the
+// backend's exp returns -inf there; so does this one.
+// kFmaReduction: f as one FMA (the backend's scalar copies, which its compiler
+// contracts) or as a multiply and a subtract (its 8-lane copy in the scan loop).
+template <bool kFmaReduction> __device__ __forceinline__ float reference_exp(float x) {
+  x = fmaxf(fminf(x, 88.3762626647949f), -88.3762626647949f);
+  const float t = __fmul_rn(x, 1.44269504089f);
+  const float tf = floorf(t);
+  const float f = kFmaReduction ? __fmaf_rn(-tf, 0.6931471805599453f, x)
+                                : __fsub_rn(x, __fmul_rn(tf, 0.6931471805599453f));
+  float p = __fmaf_rn(0.008333333333f, f, 0.041666666666f);
+  p = __fmaf_rn(p, f, 0.166666666666f);
+  p = __fmaf_rn(p, f, 0.5f);
+  p = __fmaf_rn(p, f, 1.0f);
+  p = __fmaf_rn(p, f, 1.0f);
+  const unsigned bits = static_cast<unsigned>(static_cast<int>(tf) + 127) << 23;
+  return __fmul_rn(p, __uint_as_float(bits));
+}
+
 // softplus(x + bias) = log(1 + e^(x+bias)).
 // Exact variants: IEEE expf/log1pf with the reference's branches
 // (cc:137-143: x > 20 -> x, x < -20 -> e^x).
@@ -218,6 +260,17 @@ __device__ __forceinline__ float softplus(float x, float bias, float bias_l2e) {
 template <bool kExactMath> __device__ __forceinline__ float silu(float x) {
   if (kExactMath) return x / (1.f + expf(-x));
   return x * rcp_approx(1.f + ex2_approx(x * -1.4426950408889634f));
+}
+
+// The reference backend's softplus and SiLU (cc:137-148): its own exp (the
+// scalar, FMA-reduced copy), then log1pf, or 1 + e and an IEEE division.
+__device__ __forceinline__ float softplus_reference(float x) {
+  const float e = reference_exp<true>(x);
+  const float l = log1pf(e);
+  return x > 20.f ? x : (x < -20.f ? e : l);
+}
+__device__ __forceinline__ float silu_reference(float x) {
+  return __fdiv_rn(x, __fadd_rn(1.f, reference_exp<true>(-x)));
 }
 
 // Two consecutive steps at once: the FMA/add/multiply parts of softplus and

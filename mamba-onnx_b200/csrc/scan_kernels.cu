@@ -59,8 +59,9 @@ constexpr int kAcc = MAMBA_SCAN_ACC;
 // SFU exponentials per step bound it, so one pair moves there (Exact
 // 1x2048x16384: 312 -> 295 us); the emit pass is not SFU-bound and keeps all
 // of them on the SFU.
-template <int M> struct PolyPairs {
-  static constexpr int value = (M == kEmit) ? MAMBA_SCAN_POLY_EMIT : MAMBA_SCAN_POLY_AGG;
+template <int M, int E> struct PolyPairs {
+  static constexpr int value =
+      E != kExpSfu ? 0 : ((M == kEmit) ? MAMBA_SCAN_POLY_EMIT : MAMBA_SCAN_POLY_AGG);
 };
 
 #ifndef MAMBA_SCAN_WSCALE
@@ -79,54 +80,52 @@ template <int M> struct PolyPairs {
 // so B enters unscaled and the per-state multiply delta*u*B disappears: the
 // state update costs abar' = fma(r*delta, A, r) and one FMA, three FP32
 // operations per (row, step, state) with the contraction instead of four.
-// At the start of a pass w_{-1} = 1 (g = h), and the state leaves as
-// h = w_last * g.
+// w is kept away from zero: |w| < kWMin takes kWMin (the input term then
+// differs from w*B by at most 2*kWMin*|B|). At the start of a pass w_{-1} = 1
+// (g = h), and the state leaves as h = w_last * g. The padding steps of a
+// ragged last tile (delta = 0, B = 0) keep w and g as they are.
 //
-// g = h / w has a smaller range than h: it overflows where |w| is tiny
-// against |h| (u = 0 gives w = 0). So each 16-step tile checks, before it
-// starts, that every step of every lane of the warp has
-//   |w_t| >= tau = max(2^-40, 2^-96 * max_n |h_n|)
-// (|h| at the tile's start; the aggregate pass also counts the decay product,
-// which is kept in the same units). Then |g| stays below 2^96 times the
-// growth of h within the tile, 2^16 when |1 + delta*A| <= 2 (the reference
-// tests' large_delta regime), far inside float32's 2^128. If any lane misses
-// the bound, the whole warp runs that tile on h itself, exactly the
-// reference's form (abar = 1 + delta*A, input term delta*u*B, no division),
-// and resumes the rescaled form on the next tile with w_{-1} = 1. In the
-// benchmark distributions |delta*u| < 2^-40 needs |u| < ~1e-9, so the h-form
-// tiles appear only where u or delta is (near) zero, and on a sequence's
-// ragged last tile (its padding steps have delta = 0).
+// g = h / w has a smaller range than h: where |w| is tiny against |h| (a
+// u = 0 step in a state that has grown past ~1e26) g overflows although the
+// reference's h stays finite. An overflow cannot heal (inf times r*abar stays
+// inf or turns NaN), so each pass checks its final state (and decay product)
+// once: if any lane's is not finite, the warp runs the whole pass again on h
+// itself, exactly the reference's form (abar = 1 + delta*A, input term
+// delta*u*B, no division), and that result replaces the first one. The hot
+// loop pays nothing for this; a pass that overflows pays a second, slower
+// pass.
 //
 // The exact variants keep abar = exp(delta*A) and the product delta*u*B (a
 // positive w is not guaranteed, so r cannot be folded into the exponent).
-constexpr float kWFloor = 0x1p-40f;
-constexpr float kWRange = 0x1p-96f;
+constexpr float kWMin = 1e-12f;
+
+__device__ __forceinline__ float safe_w(float w) { return fabsf(w) < kWMin ? kWMin : w; }
 
 template <int V> struct Scaled {
   static constexpr bool value = MAMBA_SCAN_WSCALE && !VariantTraits<V>::exact;
 };
 
-// max(a, b, c) in one instruction (sm_100 three-input max).
-__device__ __forceinline__ float max3(float a, float b, float c) {
-  float m;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(m) : "f"(a), "f"(b), "f"(c));
-  return m;
-}
+template <bool B> struct BoolTag {
+  static constexpr bool value = B;
+};
 
-// max_n |x_n| over a lane's 16 state values.
-__device__ __forceinline__ float max_abs16(const float2 (&x)[8]) {
-  float m = fmaxf(fabsf(x[0].x), fabsf(x[0].y));
+// True when all 16 values of a lane's state are finite (their sum is: an
+// infinite or NaN element makes it so, and a sum that overflows only sends a
+// finite state to the slower pass).
+__device__ __forceinline__ bool finite16(const float2 (&x)[8]) {
+  float2 s = add2(x[0], x[1]);
 #pragma unroll
-  for (int n = 1; n < 8; ++n) m = max3(m, fabsf(x[n].x), fabsf(x[n].y));
-  return m;
+  for (int n = 2; n < 8; ++n) s = add2(s, x[n]);
+  return isfinite(s.x + s.y);
 }
 
 // abar and the input term of one step, for the lane's 16 states.
-// Exact variants: (x0, x1) = (delta, delta*u); a = exp(delta*A), bu = delta*u*B.
+// Exact variants: (x0, x1) = (delta, delta*u); a = exp(delta*A) formed as the
+// exp mode E says, bu = delta*u*B.
 // Linear variants, rescaled (kScaled): (x0, x1) = (r*delta, r),
 // a = r*(1 + delta*A), bu = B; on h itself: (x0, x1) = (delta, delta*u),
 // a = 1 + delta*A, bu = delta*u*B.
-template <int V, int M, bool kScaled>
+template <int V, int M, bool kScaled, int E>
 __device__ __forceinline__ void step_prep(const float* __restrict__ Bt_, float x0_, float x1_,
                                           const float2 (&Ar)[8], float2 (&a)[8], float2 (&bu)[8]) {
   using Tr = VariantTraits<V>;
@@ -137,15 +136,27 @@ __device__ __forceinline__ void step_prep(const float* __restrict__ Bt_, float x
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     const float4 bq = Bt[q];
-    if (Tr::exact) {
+    if (Tr::exact && E == kExpSfu) {
       // abar = exp(delta*A) = 2^(delta * A*log2(e)); Ar holds A*log2(e)
       const float2 x0 = mul2(dt2, Ar[2 * q]);
       const float2 x1 = mul2(dt2, Ar[2 * q + 1]);
-      a[2 * q] = (2 * q < PolyPairs<M>::value) ? exp2_fma2(x0)
-                                               : make_float2(ex2_approx(x0.x), ex2_approx(x0.y));
-      a[2 * q + 1] = (2 * q + 1 < PolyPairs<M>::value)
+      a[2 * q] = (2 * q < PolyPairs<M, E>::value)
+                     ? exp2_fma2(x0)
+                     : make_float2(ex2_approx(x0.x), ex2_approx(x0.y));
+      a[2 * q + 1] = (2 * q + 1 < PolyPairs<M, E>::value)
                          ? exp2_fma2(x1)
                          : make_float2(ex2_approx(x1.x), ex2_approx(x1.y));
+    } else if (Tr::exact && E == kExpIeee) {
+      const float2 x0 = mul2(dt2, Ar[2 * q]);  // Ar holds A
+      const float2 x1 = mul2(dt2, Ar[2 * q + 1]);
+      a[2 * q] = make_float2(expf(x0.x), expf(x0.y));
+      a[2 * q + 1] = make_float2(expf(x1.x), expf(x1.y));
+    } else if (Tr::exact) {
+      // the reference's 8-lane exp (cc:265-268: delta*A, then fast_exp_avx2)
+      const float2 x0 = mul2(dt2, Ar[2 * q]);
+      const float2 x1 = mul2(dt2, Ar[2 * q + 1]);
+      a[2 * q] = make_float2(reference_exp<false>(x0.x), reference_exp<false>(x0.y));
+      a[2 * q + 1] = make_float2(reference_exp<false>(x1.x), reference_exp<false>(x1.y));
     } else if (kScaled) {
       // abar' = r*(1 + delta*A) = fma(r*delta, A, r)
       a[2 * q] = fma2(dt2, Ar[2 * q], du2);
@@ -188,8 +199,8 @@ __device__ __forceinline__ float2 contract(const float* __restrict__ Ct_, const 
 // Per-step scalar work of one 16-step tile for the calling lane's row, on
 // packed pairs of consecutive steps (entry k holds steps 2k and 2k+1):
 //   dt, du  (delta, delta*u); on the rescaled state of the linear variants
-//           (r*delta, r) with r_t = w_{t-1} / w_t (see rescale_scalars);
-//   ww      w = delta*u (rescaled state);
+//           (r*delta, r) with r_t = w_{t-1} / w_t;
+//   ww      w = delta*u kept away from zero (rescaled state);
 //   dsk     D*u (rescaled state, emit); uu: u; gate: silu(z) (fused, emit).
 // Softplus (fused variants) is applied to delta first; kPartial zeroes delta
 // of the steps >= n_valid (the ragged last tile).
@@ -197,12 +208,14 @@ struct TileScalars {
   float2 uu[8], dt[8], du[8], gate[8], ww[8], dsk[8];
 };
 
-template <int V, int M, bool kPartial>
+template <int V, int M, bool kPartial, int E, bool kScaled>
 __device__ __forceinline__ void tile_scalars(const float* us, const float* __restrict__ ds,
-                                             const float* __restrict__ zs, int row, float bias,
-                                             float bias_l2e, int n_valid, TileScalars& ts) {
+                                             const float* __restrict__ zs, int row, float dskip,
+                                             float bias, float bias_l2e, int n_valid,
+                                             float& w_prev, TileScalars& ts) {
   using Tr = VariantTraits<V>;
   const float2 bias_l2e2 = make_float2(bias_l2e, bias_l2e);
+  const float2 dskip2 = make_float2(dskip, dskip);
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
     const int off = row * kT + (((c ^ (row >> 1)) & 3) << 2);
@@ -212,7 +225,17 @@ __device__ __forceinline__ void tile_scalars(const float* us, const float* __res
     ts.uu[2 * c + 1] = make_float2(u4.z, u4.w);
     ts.dt[2 * c] = make_float2(d4.x, d4.y);
     ts.dt[2 * c + 1] = make_float2(d4.z, d4.w);
-    if (Tr::fused) {
+    if (Tr::fused && E == kExpReference) {
+      // the reference backend's softplus and SiLU (cc:137-148)
+      ts.dt[2 * c] = make_float2(softplus_reference(d4.x + bias), softplus_reference(d4.y + bias));
+      ts.dt[2 * c + 1] =
+          make_float2(softplus_reference(d4.z + bias), softplus_reference(d4.w + bias));
+      if (M == kEmit) {
+        const float4 z4 = *reinterpret_cast<const float4*>(zs + off);
+        ts.gate[2 * c] = make_float2(silu_reference(z4.x), silu_reference(z4.y));
+        ts.gate[2 * c + 1] = make_float2(silu_reference(z4.z), silu_reference(z4.w));
+      }
+    } else if (Tr::fused) {
       ts.dt[2 * c] = softplus2<Tr::exact>(ts.dt[2 * c], bias, bias_l2e2);
       ts.dt[2 * c + 1] = softplus2<Tr::exact>(ts.dt[2 * c + 1], bias, bias_l2e2);
       if (M == kEmit) {
@@ -231,22 +254,29 @@ __device__ __forceinline__ void tile_scalars(const float* us, const float* __res
   }
 #pragma unroll
   for (int k = 0; k < 8; ++k) ts.du[k] = mul2(ts.dt[k], ts.uu[k]);
-}
-
-// Rescaled state of the linear variants: from here dt holds r*delta, du
-// holds r, ww holds w = delta*u, dsk holds D*u. Every |w| of the tile is at
-// least tau > 0 (checked by the caller), so the reciprocal is finite.
-template <int M>
-__device__ __forceinline__ void rescale_scalars(float dskip, float& w_prev, TileScalars& ts) {
-  const float2 dskip2 = make_float2(dskip, dskip);
+  // Linear variants on the rescaled state: from here dt holds r*delta, du
+  // holds r, and ww holds w = delta*u (kept away from zero). A padding step
+  // gets w = w_{t-1}, r = 1 and r*delta = 0: abar' = 1 and its B is zero.
+  if (kScaled) {
 #pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    ts.ww[k] = ts.du[k];
-    const float2 inv = make_float2(rcp_approx(ts.ww[k].x), rcp_approx(ts.ww[k].y));
-    ts.du[k] = make_float2(w_prev * inv.x, ts.ww[k].x * inv.y);  // r = w_{t-1} / w_t
-    w_prev = ts.ww[k].y;
-    ts.dt[k] = mul2(ts.du[k], ts.dt[k]);
-    if (M == kEmit) ts.dsk[k] = mul2(dskip2, ts.uu[k]);
+    for (int k = 0; k < 8; ++k) {
+      ts.ww[k] = make_float2(safe_w(ts.du[k].x), safe_w(ts.du[k].y));
+      const float2 inv = make_float2(rcp_approx(ts.ww[k].x), rcp_approx(ts.ww[k].y));
+      ts.du[k] = make_float2(w_prev * inv.x, ts.ww[k].x * inv.y);  // r = w_{t-1} / w_t
+      if (kPartial) {
+        if (2 * k >= n_valid) {
+          ts.ww[k].x = w_prev;
+          ts.du[k].x = 1.f;
+        }
+        if (2 * k + 1 >= n_valid) {
+          ts.ww[k].y = ts.ww[k].x;
+          ts.du[k].y = 1.f;
+        }
+      }
+      w_prev = ts.ww[k].y;
+      ts.dt[k] = mul2(ts.du[k], ts.dt[k]);
+      if (M == kEmit) ts.dsk[k] = mul2(dskip2, ts.uu[k]);
+    }
   }
 }
 
@@ -265,27 +295,44 @@ __device__ __forceinline__ float2 step_pair_output(const TileScalars& ts, int k,
   return Tr::fused ? mul2(y, ts.gate[k]) : y;
 }
 
-// The state loop of one 16-step tile (row-per-lane layout: the lane keeps all
-// 16 states of its row in h[0..7]): updates h (and the decay product P, or
-// the delta sum S, in aggregate mode) and, in emit mode, leaves the tile's
-// outputs in yy. abar and the input term of step t+1 are formed before the
-// C.h contraction of step t, so the contraction overlaps the next step's
+// One 16-step tile for the calling lane's row (row-per-lane layout: the lane
+// keeps all 16 states of its row in h[0..7]). Reads the swizzled u/delta/z
+// tiles and the B/C tiles, updates h (and the decay product P, or the delta
+// sum S, in aggregate mode) and, in emit mode, writes y into the swizzled
+// output tile `os` (which may be the u tile itself: every u value is read
+// before the first output is written). kScaled: the linear variants'
+// rescaled state (false: h itself).
+//
+// The per-step scalar work is done first for all 16 steps (tile_scalars).
+// The state loop then computes abar and the input term of step t+1 before
+// the C.h contraction of step t, so the contraction overlaps the next step's
 // independent work.
-template <int V, int M, bool kScaled>
-__device__ __forceinline__ void state_loop(const TileScalars& ts, const float* __restrict__ Bs,
-                                           const float* __restrict__ Cs, float2 (&h)[8],
-                                           float2 (&P)[8], float& S, const float2 (&Ar)[8],
-                                           float dskip, float2 (&yy)[8]) {
+template <int V, int M, bool kPartial, int E, bool kScaled>
+__device__ __forceinline__ void compute_tile(const float* us,
+                                             const float* __restrict__ ds,
+                                             const float* __restrict__ zs,
+                                             const float* __restrict__ Bs,
+                                             const float* __restrict__ Cs, float* os,
+                                             int row, float2 (&h)[8], float2 (&P)[8], float& S,
+                                             const float2 (&Ar)[8], float dskip, float bias,
+                                             float bias_l2e, int n_valid, float& w_prev) {
   using Tr = VariantTraits<V>;
+  TileScalars ts;
+  tile_scalars<V, M, kPartial, E, kScaled>(us, ds, zs, row, dskip, bias, bias_l2e, n_valid,
+                                           w_prev, ts);
   float2 a[8], bu[8];
-  step_prep<V, M, kScaled>(Bs, ts.dt[0].x, ts.du[0].x, Ar, a, bu);
+  step_prep<V, M, kScaled, E>(Bs, ts.dt[0].x, ts.du[0].x, Ar, a, bu);
   float2 s_prev = make_float2(0.f, 0.f);
+  float2 yy[8];
 #pragma unroll
   for (int t = 0; t < kT; ++t) {
 #pragma unroll
     for (int n = 0; n < 8; ++n) h[n] = fma2(a[n], h[n], bu[n]);
     if (M == kAggregate) {
-      if (!Tr::exact) {
+      // the chunk's decay: the product of the abar (linear variants, and the
+      // reference exp, whose product is what the backend's recurrence
+      // applies), else exp(A * sum(delta)) at the chunk's end
+      if (!Tr::exact || E == kExpReference) {
 #pragma unroll
         for (int n = 0; n < 8; ++n) P[n] = mul2(P[n], a[n]);
       } else {
@@ -294,8 +341,8 @@ __device__ __forceinline__ void state_loop(const TileScalars& ts, const float* _
     }
     if (t + 1 < kT) {
       const int k = (t + 1) >> 1;
-      step_prep<V, M, kScaled>(Bs + (t + 1) * kN, ((t + 1) & 1) ? ts.dt[k].y : ts.dt[k].x,
-                               ((t + 1) & 1) ? ts.du[k].y : ts.du[k].x, Ar, a, bu);
+      step_prep<V, M, kScaled, E>(Bs + (t + 1) * kN, ((t + 1) & 1) ? ts.dt[k].y : ts.dt[k].x,
+                                  ((t + 1) & 1) ? ts.du[k].y : ts.du[k].x, Ar, a, bu);
     }
     if (M == kEmit) {
       const float2 s = contract(Cs + t * kN, h);
@@ -305,54 +352,6 @@ __device__ __forceinline__ void state_loop(const TileScalars& ts, const float* _
       else
         s_prev = s;
     }
-  }
-}
-
-// One 16-step tile for the calling lane's row. Reads the swizzled u/delta/z
-// tiles and the B/C tiles, runs the state loop and, in emit mode, writes y
-// into the swizzled output tile `os` (which may be the u tile itself: every
-// u value is read before the first output is written).
-//
-// The per-step scalar work is done first for all 16 steps (tile_scalars).
-// The linear variants then choose, for the whole warp, between the rescaled
-// state and h itself for this tile (see Scaled above); w_prev carries the
-// scale of the rescaled state from tile to tile (1 when h and g coincide).
-template <int V, int M, bool kPartial>
-__device__ __forceinline__ void compute_tile(const float* us,
-                                             const float* __restrict__ ds,
-                                             const float* __restrict__ zs,
-                                             const float* __restrict__ Bs,
-                                             const float* __restrict__ Cs, float* os,
-                                             int row, float2 (&h)[8], float2 (&P)[8], float& S,
-                                             const float2 (&Ar)[8], float dskip, float bias,
-                                             float bias_l2e, int n_valid, float& w_prev) {
-  TileScalars ts;
-  tile_scalars<V, M, kPartial>(us, ds, zs, row, bias, bias_l2e, n_valid, ts);
-  float2 yy[8];
-  if (Scaled<V>::value) {
-    float hmax = max_abs16(h);
-    if (M == kAggregate) hmax = fmaxf(hmax, max_abs16(P));
-    const float tau = fmaxf(kWFloor, hmax * fabsf(w_prev) * kWRange);
-    bool small = false;
-#pragma unroll
-    for (int k = 0; k < 8; ++k) small = small || !(fabsf(ts.du[k].x) >= tau) ||
-                                        !(fabsf(ts.du[k].y) >= tau);
-    if (!__any_sync(0xffffffffu, small)) {
-      rescale_scalars<M>(dskip, w_prev, ts);
-      state_loop<V, M, true>(ts, Bs, Cs, h, P, S, Ar, dskip, yy);
-    } else {
-      // this tile on h itself: g -> h (and the decay to the same units)
-      const float2 wp = make_float2(w_prev, w_prev);
-#pragma unroll
-      for (int n = 0; n < 8; ++n) {
-        h[n] = mul2(h[n], wp);
-        if (M == kAggregate) P[n] = mul2(P[n], wp);
-      }
-      w_prev = 1.f;
-      state_loop<V, M, false>(ts, Bs, Cs, h, P, S, Ar, dskip, yy);
-    }
-  } else {
-    state_loop<V, M, false>(ts, Bs, Cs, h, P, S, Ar, dskip, yy);
   }
   if (M == kEmit) {
 #pragma unroll
@@ -416,88 +415,210 @@ __device__ __forceinline__ void store_tile_plain(const float* os, const ScanPara
 #define MAMBA_SCAN_MIN_BLOCKS 8
 #endif
 
-template <int V, int M, bool kTma>
-__global__ void __launch_bounds__(kRows, MAMBA_SCAN_MIN_BLOCKS)
-    scan_kernel(const ScanParams p, const __grid_constant__ TmaMaps maps) {
-  using Tr = VariantTraits<V>;
-  __shared__ TileSmem sm;
-  // The carry kernel (launched next, programmatic dependent launch) may be
-  // scheduled right away; it waits for this grid to finish before reading.
-  if (M == kAggregate) pdl_trigger();
+// Which row tile and which part of the sequence a CTA owns.
+struct CtaWork {
+  int rt, chunk, n_chunks, n_tiles, b, d0;
+  int64_t l_begin, l_end;
+};
 
-  const int lane = threadIdx.x;
-  // Which row tile and which part of the sequence this CTA owns.
-  int rt, chunk, n_chunks;
+template <int M> __device__ __forceinline__ CtaWork cta_work(const ScanParams& p) {
+  CtaWork w;
   if (M == kEmit && (int)blockIdx.x < p.n_full) {
-    rt = blockIdx.x;  // whole sequence in one pass
-    chunk = 0;
-    n_chunks = 1;
+    w.rt = blockIdx.x;  // whole sequence in one pass
+    w.chunk = 0;
+    w.n_chunks = 1;
   } else {
     const int j = (int)blockIdx.x - (M == kEmit ? p.n_full : 0);
     const int per = (M == kEmit) ? p.n_chunks : p.n_chunks - 1;
-    rt = p.n_full + j / per;
-    chunk = j % per;
-    n_chunks = p.n_chunks;
+    w.rt = p.n_full + j / per;
+    w.chunk = j % per;
+    w.n_chunks = p.n_chunks;
   }
-  const int64_t l_begin = (int64_t)chunk * p.chunk_len;
-  const int64_t l_end = (chunk == n_chunks - 1) ? p.seqlen : l_begin + p.chunk_len;
-  const int n_tiles = (int)((l_end - l_begin + kT - 1) / kT);
-  const int b = rt / p.tiles_per_batch;
-  const int d0 = (rt - b * p.tiles_per_batch) * kRows;
+  w.l_begin = (int64_t)w.chunk * p.chunk_len;
+  w.l_end = (w.chunk == w.n_chunks - 1) ? p.seqlen : w.l_begin + p.chunk_len;
+  w.n_tiles = (int)((w.l_end - w.l_begin + kT - 1) / kT);
+  w.b = w.rt / p.tiles_per_batch;
+  w.d0 = (w.rt - w.b * p.tiles_per_batch) * kRows;
+  return w;
+}
 
-  const int d = d0 + lane;
-  const bool row_ok = d < p.dim;
-  const int64_t dc = row_ok ? d : p.dim - 1;  // clamped: parameter loads stay in bounds
-  const int64_t row = (int64_t)b * p.dim + dc;
-  // this lane's slot among the split rows' aggregates
-  const int64_t ws_row = (int64_t)(rt - p.n_full) * kRows + lane;
-
-  // Per-row constants: A (scaled by log2(e) for the exp2-based exact
-  // variants), the D skip weight, the optional delta bias.
+// The calling lane's row and its constants: A (scaled by log2(e) for the
+// exact variants' SFU exp2), the D skip weight, the optional delta bias.
+struct RowConsts {
   float2 Ar[8];
+  float dskip, bias, bias_l2e;
+  int64_t row;     // b*dim + d (d clamped to the last row for padding lanes)
+  int64_t ws_row;  // this lane's slot among the split rows' aggregates
+  bool row_ok;     // d < dim
+};
+
+template <int V, int E>
+__device__ __forceinline__ void row_consts(const ScanParams& p, const CtaWork& w, int lane,
+                                           RowConsts& rc) {
+  using Tr = VariantTraits<V>;
+  const int d = w.d0 + lane;
+  rc.row_ok = d < p.dim;
+  const int64_t dc = rc.row_ok ? d : p.dim - 1;  // clamped: parameter loads stay in bounds
+  rc.row = (int64_t)w.b * p.dim + dc;
+  rc.ws_row = (int64_t)(w.rt - p.n_full) * kRows + lane;
 #pragma unroll
   for (int n = 0; n < 8; ++n) {
     float a0 = __ldg(p.A + dc * kN + 2 * n), a1 = __ldg(p.A + dc * kN + 2 * n + 1);
-    if (Tr::exact) {
+    if (Tr::exact && E == kExpSfu) {
       a0 *= 1.4426950408889634f;
       a1 *= 1.4426950408889634f;
     }
-    Ar[n] = make_float2(a0, a1);
+    rc.Ar[n] = make_float2(a0, a1);
   }
-  const float dskip = __ldg(p.D + dc);
-  const float bias = (Tr::fused && p.delta_bias != nullptr) ? __ldg(p.delta_bias + dc) : 0.f;
-  const float bias_l2e = bias * 1.4426950408889634f;
+  rc.dskip = __ldg(p.D + dc);
+  rc.bias = (Tr::fused && p.delta_bias != nullptr) ? __ldg(p.delta_bias + dc) : 0.f;
+  rc.bias_l2e = rc.bias * 1.4426950408889634f;
+}
 
-  // Initial state: zeros (cc:241-242) or h0; emit chunks > 0 start from the
-  // carry-in state of the chunks before them.
-  float2 h[8], P[8];
-  float S = 0.f;
-  float w_prev = 1.f;  // linear variants: the state runs as g = h / w (w_{-1} = 1)
+// Initial state: zeros (cc:241-242) or h0; emit chunks > 0 start from the
+// carry-in state of the chunks before them. w_prev = 1: g = h at the start.
+template <int M>
+__device__ __forceinline__ void init_state(const ScanParams& p, const CtaWork& w,
+                                           const RowConsts& rc, float2 (&h)[8], float2 (&P)[8],
+                                           float& S, float& w_prev) {
+  S = 0.f;
+  w_prev = 1.f;
 #pragma unroll
   for (int n = 0; n < 8; ++n) {
     h[n] = make_float2(0.f, 0.f);
     P[n] = make_float2(1.f, 1.f);
   }
   if (M == kEmit) {
-    if (chunk > 0) {
+    if (w.chunk > 0) {
       // The state entering this chunk, folded by carry_kernel (launched
       // between the two passes; wait for it and, through it, the aggregate
       // pass). Whole row tiles and first chunks do not wait.
       pdl_wait();
-      const float4* w = reinterpret_cast<const float4*>(
-          p.ws + (ws_row * (int64_t)(n_chunks - 1) + chunk - 1) * 2 * kN);
+      const float4* ws = reinterpret_cast<const float4*>(
+          p.ws + (rc.ws_row * (int64_t)(w.n_chunks - 1) + w.chunk - 1) * 2 * kN);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        const float4 e = __ldcg(w + q);
+        const float4 e = __ldcg(ws + q);
         h[2 * q] = make_float2(e.x, e.y);
         h[2 * q + 1] = make_float2(e.z, e.w);
       }
     } else if (p.h0 != nullptr) {
 #pragma unroll
       for (int n = 0; n < 8; ++n)
-        h[n] = make_float2(__ldg(p.h0 + row * kN + 2 * n), __ldg(p.h0 + row * kN + 2 * n + 1));
+        h[n] = make_float2(__ldg(p.h0 + rc.row * kN + 2 * n),
+                           __ldg(p.h0 + rc.row * kN + 2 * n + 1));
     }
   }
+}
+
+// One pass over a CTA's tiles with plain loads and stores (stage 0 of the
+// ring). kScaled: the linear variants' rescaled state, or h itself.
+// kOneForm: every tile through the ragged-tile code (less code for a pass
+// that runs rarely).
+template <int V, int M, int E, bool kScaled, bool kOneForm = false>
+__device__ __forceinline__ void plain_pass(TileSmem& sm, const ScanParams& p, const CtaWork& w,
+                                           int lane, const RowConsts& rc, float2 (&h)[8],
+                                           float2 (&P)[8], float& S, float& w_prev) {
+  for (int k = 0; k < w.n_tiles; ++k) {
+    const int64_t t0 = w.l_begin + (int64_t)k * kT;
+    load_tile_plain<V, M>(sm, p, w.b, w.d0, t0, lane);
+    __syncwarp();
+    const int n_valid = (w.l_end - t0 < kT) ? (int)(w.l_end - t0) : kT;
+    float* os = sm.u[0];
+    if (n_valid == kT && !kOneForm)
+      compute_tile<V, M, false, E, kScaled>(sm.u[0], sm.dl[0], sm.z[0], sm.B[0], sm.C[0], os,
+                                            lane, h, P, S, rc.Ar, rc.dskip, rc.bias, rc.bias_l2e,
+                                            n_valid, w_prev);
+    else
+      compute_tile<V, M, true, E, kScaled>(sm.u[0], sm.dl[0], sm.z[0], sm.B[0], sm.C[0], os,
+                                           lane, h, P, S, rc.Ar, rc.dskip, rc.bias, rc.bias_l2e,
+                                           n_valid, w_prev);
+    __syncwarp();
+    if (M == kEmit) store_tile_plain(os, p, w.b, w.d0, t0, lane);
+    __syncwarp();
+  }
+}
+
+// End of a pass: the state back to h (and, for the aggregates, prod(abar));
+// the final state to h_last (emit, last chunk) or the chunk's end state and
+// decay to the workspace (aggregate).
+template <int V, int M, int E>
+__device__ __forceinline__ void finish_pass(const ScanParams& p, const CtaWork& w,
+                                            const RowConsts& rc, float2 (&h)[8], float2 (&P)[8],
+                                            float S, float w_prev) {
+  using Tr = VariantTraits<V>;
+  if (!rc.row_ok) return;
+  if (Scaled<V>::value) {
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      h[n] = mul2(h[n], make_float2(w_prev, w_prev));
+      P[n] = mul2(P[n], make_float2(w_prev, w_prev));
+    }
+  }
+  if (M == kEmit) {
+    if (p.h_last != nullptr && w.chunk == w.n_chunks - 1) {
+#pragma unroll
+      for (int n = 0; n < 8; ++n) {
+        p.h_last[rc.row * kN + 2 * n] = h[n].x;
+        p.h_last[rc.row * kN + 2 * n + 1] = h[n].y;
+      }
+    }
+  } else {
+    // 32 floats per (row, chunk): the end state, then the decay.
+    float4* ws = reinterpret_cast<float4*>(
+        p.ws + (rc.ws_row * (int64_t)(w.n_chunks - 1) + w.chunk) * 2 * kN);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float2 p0 = P[2 * q], p1 = P[2 * q + 1];
+      if (Tr::exact && E == kExpSfu) {
+        p0 = make_float2(ex2_approx(rc.Ar[2 * q].x * S), ex2_approx(rc.Ar[2 * q].y * S));
+        p1 = make_float2(ex2_approx(rc.Ar[2 * q + 1].x * S),
+                         ex2_approx(rc.Ar[2 * q + 1].y * S));
+      } else if (Tr::exact && E == kExpIeee) {
+        p0 = make_float2(expf(rc.Ar[2 * q].x * S), expf(rc.Ar[2 * q].y * S));
+        p1 = make_float2(expf(rc.Ar[2 * q + 1].x * S), expf(rc.Ar[2 * q + 1].y * S));
+      }
+      ws[q] = make_float4(h[2 * q].x, h[2 * q].y, h[2 * q + 1].x, h[2 * q + 1].y);
+      ws[4 + q] = make_float4(p0.x, p0.y, p1.x, p1.y);
+    }
+  }
+}
+
+// The CTA's whole pass again, on h itself (the reference's form), for a warp
+// whose rescaled state overflowed; writes every output of the pass again and
+// finishes it. (Kept inline: an out-of-line call made the hot loop slower.)
+template <int V, int M, int E>
+__device__ __forceinline__ void rerun_on_h(const ScanParams& p, TileSmem& sm, int lane) {
+  const CtaWork w = cta_work<M>(p);
+  RowConsts rc;
+  row_consts<V, E>(p, w, lane, rc);
+  float2 h[8], P[8];
+  float S, w_prev;
+  init_state<M>(p, w, rc, h, P, S, w_prev);
+  plain_pass<V, M, E, false, true>(sm, p, w, lane, rc, h, P, S, w_prev);
+  finish_pass<V, M, E>(p, w, rc, h, P, S, 1.f);
+}
+
+template <int V, int M, bool kTma, int E>
+__global__ void __launch_bounds__(kRows, MAMBA_SCAN_MIN_BLOCKS)
+    scan_kernel(const __grid_constant__ ScanParams p, const __grid_constant__ TmaMaps maps) {
+  using Tr = VariantTraits<V>;
+  constexpr bool kScaled = Scaled<V>::value;
+  __shared__ TileSmem sm;
+  // The carry kernel (launched next, programmatic dependent launch) may be
+  // scheduled right away; it waits for this grid to finish before reading.
+  if (M == kAggregate) pdl_trigger();
+
+  const int lane = threadIdx.x;
+  const CtaWork w = cta_work<M>(p);
+  RowConsts rc;
+  row_consts<V, E>(p, w, lane, rc);
+  float2 h[8], P[8];
+  float S, w_prev;  // w_prev: linear variants run the state as g = h / w
+  init_state<M>(p, w, rc, h, P, S, w_prev);
+  const int b = w.b, d0 = w.d0;
+  const int64_t l_begin = w.l_begin, l_end = w.l_end;
+  const int n_tiles = w.n_tiles;
 
   if (kTma) {
     // bytes landing per stage: full boxes, out-of-range elements included
@@ -540,11 +661,13 @@ __global__ void __launch_bounds__(kRows, MAMBA_SCAN_MIN_BLOCKS)
       const int n_valid = (l_end - t0 < kT) ? (int)(l_end - t0) : kT;
       float* os = sm.u[s];  // outputs overwrite this tile's u
       if (n_valid == kT)
-        compute_tile<V, M, false>(sm.u[s], sm.dl[s], sm.z[s], sm.B[s], sm.C[s], os, lane, h, P, S,
-                                  Ar, dskip, bias, bias_l2e, n_valid, w_prev);
+        compute_tile<V, M, false, E, kScaled>(sm.u[s], sm.dl[s], sm.z[s], sm.B[s], sm.C[s], os,
+                                              lane, h, P, S, rc.Ar, rc.dskip, rc.bias,
+                                              rc.bias_l2e, n_valid, w_prev);
       else
-        compute_tile<V, M, true>(sm.u[s], sm.dl[s], sm.z[s], sm.B[s], sm.C[s], os, lane, h, P, S,
-                                 Ar, dskip, bias, bias_l2e, n_valid, w_prev);
+        compute_tile<V, M, true, E, kScaled>(sm.u[s], sm.dl[s], sm.z[s], sm.B[s], sm.C[s], os,
+                                             lane, h, P, S, rc.Ar, rc.dskip, rc.bias,
+                                             rc.bias_l2e, n_valid, w_prev);
       if (M == kEmit) {
         fence_proxy_async_smem();
         __syncwarp();
@@ -564,54 +687,25 @@ __global__ void __launch_bounds__(kRows, MAMBA_SCAN_MIN_BLOCKS)
     }
     if (M == kEmit && lane == 0) bulk_wait_all<0>();
   } else {
-    for (int k = 0; k < n_tiles; ++k) {
-      const int64_t t0 = l_begin + (int64_t)k * kT;
-      load_tile_plain<V, M>(sm, p, b, d0, t0, lane);
-      __syncwarp();
-      const int n_valid = (l_end - t0 < kT) ? (int)(l_end - t0) : kT;
-      float* os = sm.u[0];
-      if (n_valid == kT)
-        compute_tile<V, M, false>(sm.u[0], sm.dl[0], sm.z[0], sm.B[0], sm.C[0], os, lane,
-                                  h, P, S, Ar, dskip, bias, bias_l2e, n_valid, w_prev);
-      else
-        compute_tile<V, M, true>(sm.u[0], sm.dl[0], sm.z[0], sm.B[0], sm.C[0], os, lane,
-                                 h, P, S, Ar, dskip, bias, bias_l2e, n_valid, w_prev);
-      __syncwarp();
-      if (M == kEmit) store_tile_plain(os, p, b, d0, t0, lane);
-      __syncwarp();
-    }
+    plain_pass<V, M, E, kScaled>(sm, p, w, lane, rc, h, P, S, w_prev);
   }
 
-  if (!row_ok) return;
-  if (Scaled<V>::value) {  // back to h (and, for the aggregates, to prod(abar))
-#pragma unroll
-    for (int n = 0; n < 8; ++n) {
-      h[n] = mul2(h[n], make_float2(w_prev, w_prev));
-      P[n] = mul2(P[n], make_float2(w_prev, w_prev));
+  // The rescaled state overflows only where the reference's h is large and
+  // |delta*u| tiny (see Scaled): then this warp's whole pass runs again on h.
+  if (kScaled) {
+    const bool bad = rc.row_ok && !(finite16(h) && (M == kEmit || finite16(P)));
+    if (__any_sync(0xffffffffu, bad)) {
+      if (kTma && M == kEmit) {
+        // the first pass's TMA stores are complete (waited for above): order
+        // them before the second pass's stores of the same outputs
+        if (lane == 0) fence_proxy_async();
+        __syncwarp();
+      }
+      rerun_on_h<V, M, E>(p, sm, lane);
+      return;
     }
   }
-  if (M == kEmit) {
-    if (p.h_last != nullptr && chunk == n_chunks - 1) {
-#pragma unroll
-      for (int n = 0; n < 8; ++n) {
-        p.h_last[row * kN + 2 * n] = h[n].x;
-        p.h_last[row * kN + 2 * n + 1] = h[n].y;
-      }
-    }
-  } else {
-    // 32 floats per (row, chunk): the end state, then the decay.
-    float4* w = reinterpret_cast<float4*>(p.ws + (ws_row * (int64_t)(n_chunks - 1) + chunk) * 2 * kN);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      float2 p0 = P[2 * q], p1 = P[2 * q + 1];
-      if (Tr::exact) {
-        p0 = make_float2(ex2_approx(Ar[2 * q].x * S), ex2_approx(Ar[2 * q].y * S));
-        p1 = make_float2(ex2_approx(Ar[2 * q + 1].x * S), ex2_approx(Ar[2 * q + 1].y * S));
-      }
-      w[q] = make_float4(h[2 * q].x, h[2 * q].y, h[2 * q + 1].x, h[2 * q + 1].y);
-      w[4 + q] = make_float4(p0.x, p0.y, p1.x, p1.y);
-    }
-  }
+  finish_pass<V, M, E>(p, w, rc, h, P, S, w_prev);
 }
 
 // ------------------------------------------------------------ carry kernel
@@ -704,24 +798,38 @@ static cudaError_t launch(void (*kernel)(Args...), unsigned blocks, unsigned thr
   return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
-template <int V>
-static cudaError_t launch_v(int mode, bool tma, const ScanParams& p, const TmaMaps& maps,
-                            unsigned blocks, cudaStream_t st, bool pdl) {
+template <int V, int E>
+static cudaError_t launch_ve(int mode, bool tma, const ScanParams& p, const TmaMaps& maps,
+                             unsigned blocks, cudaStream_t st, bool pdl) {
   if (mode == kLaunchEmit)
-    return tma ? launch(scan_kernel<V, kEmit, true>, blocks, kRows, st, pdl, p, maps)
-               : launch(scan_kernel<V, kEmit, false>, blocks, kRows, st, pdl, p, maps);
-  return tma ? launch(scan_kernel<V, kAggregate, true>, blocks, kRows, st, pdl, p, maps)
-             : launch(scan_kernel<V, kAggregate, false>, blocks, kRows, st, pdl, p, maps);
+    return tma ? launch(scan_kernel<V, kEmit, true, E>, blocks, kRows, st, pdl, p, maps)
+               : launch(scan_kernel<V, kEmit, false, E>, blocks, kRows, st, pdl, p, maps);
+  return tma ? launch(scan_kernel<V, kAggregate, true, E>, blocks, kRows, st, pdl, p, maps)
+             : launch(scan_kernel<V, kAggregate, false, E>, blocks, kRows, st, pdl, p, maps);
 }
 
-cudaError_t launch_scan_kernel(int variant, int mode, bool tma, const ScanParams& p,
-                               const TmaMaps& maps, unsigned grid, cudaStream_t stream,
-                               bool pdl) {
+template <int V>
+static cudaError_t launch_v(int mode, bool tma, int exp_mode, const ScanParams& p,
+                            const TmaMaps& maps, unsigned blocks, cudaStream_t st, bool pdl) {
+  if constexpr (!VariantTraits<V>::exact) {
+    return launch_ve<V, kExpSfu>(mode, tma, p, maps, blocks, st, pdl);
+  } else {
+    if (exp_mode == kExpIeee) return launch_ve<V, kExpIeee>(mode, tma, p, maps, blocks, st, pdl);
+    if (exp_mode == kExpReference)
+      return launch_ve<V, kExpReference>(mode, tma, p, maps, blocks, st, pdl);
+    return launch_ve<V, kExpSfu>(mode, tma, p, maps, blocks, st, pdl);
+  }
+}
+
+cudaError_t launch_scan_kernel(int variant, int exp_mode, int mode, bool tma,
+                               const ScanParams& p, const TmaMaps& maps, unsigned grid,
+                               cudaStream_t stream, bool pdl) {
   switch (variant) {
-    case kLinear: return launch_v<kLinear>(mode, tma, p, maps, grid, stream, pdl);
-    case kExact: return launch_v<kExact>(mode, tma, p, maps, grid, stream, pdl);
-    case kFused: return launch_v<kFused>(mode, tma, p, maps, grid, stream, pdl);
-    case kFusedExact: return launch_v<kFusedExact>(mode, tma, p, maps, grid, stream, pdl);
+    case kLinear: return launch_v<kLinear>(mode, tma, exp_mode, p, maps, grid, stream, pdl);
+    case kExact: return launch_v<kExact>(mode, tma, exp_mode, p, maps, grid, stream, pdl);
+    case kFused: return launch_v<kFused>(mode, tma, exp_mode, p, maps, grid, stream, pdl);
+    case kFusedExact:
+      return launch_v<kFusedExact>(mode, tma, exp_mode, p, maps, grid, stream, pdl);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -736,25 +844,36 @@ cudaError_t launch_carry_kernel(const ScanParams& p, cudaStream_t stream) {
   return launch(carry_kernel<32>, blocks, kCarryThreads, stream, true, p);
 }
 
-template <int V>
-static cudaError_t occupancy_v(int mode, bool tma, int* blocks) {
+template <int V, int E>
+static cudaError_t occupancy_ve(int mode, bool tma, int* blocks) {
   if (mode == kLaunchEmit)
-    return tma ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks, scan_kernel<V, kEmit, true>,
-                                                               kRows, 0)
-               : cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks, scan_kernel<V, kEmit, false>,
-                                                               kRows, 0);
+    return tma ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                     blocks, scan_kernel<V, kEmit, true, E>, kRows, 0)
+               : cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                     blocks, scan_kernel<V, kEmit, false, E>, kRows, 0);
   return tma ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-                   blocks, scan_kernel<V, kAggregate, true>, kRows, 0)
+                   blocks, scan_kernel<V, kAggregate, true, E>, kRows, 0)
              : cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-                   blocks, scan_kernel<V, kAggregate, false>, kRows, 0);
+                   blocks, scan_kernel<V, kAggregate, false, E>, kRows, 0);
 }
 
-cudaError_t max_blocks_per_sm(int variant, int mode, bool tma, int* blocks) {
+template <int V>
+static cudaError_t occupancy_v(int mode, bool tma, int exp_mode, int* blocks) {
+  if constexpr (!VariantTraits<V>::exact) {
+    return occupancy_ve<V, kExpSfu>(mode, tma, blocks);
+  } else {
+    if (exp_mode == kExpIeee) return occupancy_ve<V, kExpIeee>(mode, tma, blocks);
+    if (exp_mode == kExpReference) return occupancy_ve<V, kExpReference>(mode, tma, blocks);
+    return occupancy_ve<V, kExpSfu>(mode, tma, blocks);
+  }
+}
+
+cudaError_t max_blocks_per_sm(int variant, int exp_mode, int mode, bool tma, int* blocks) {
   switch (variant) {
-    case kLinear: return occupancy_v<kLinear>(mode, tma, blocks);
-    case kExact: return occupancy_v<kExact>(mode, tma, blocks);
-    case kFused: return occupancy_v<kFused>(mode, tma, blocks);
-    case kFusedExact: return occupancy_v<kFusedExact>(mode, tma, blocks);
+    case kLinear: return occupancy_v<kLinear>(mode, tma, exp_mode, blocks);
+    case kExact: return occupancy_v<kExact>(mode, tma, exp_mode, blocks);
+    case kFused: return occupancy_v<kFused>(mode, tma, exp_mode, blocks);
+    case kFusedExact: return occupancy_v<kFusedExact>(mode, tma, exp_mode, blocks);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -54,9 +54,11 @@ enum LaunchMode { kLaunchEmit = 0, kLaunchAggregate = 1 };
 // on `stream` with a 1-D grid of `blocks` CTAs: n_full + n_tail * n_chunks
 // for emit, n_tail * (n_chunks - 1) for aggregate. `pdl`: programmatic
 // dependent launch (the emit pass after the carry kernel).
-cudaError_t launch_scan_kernel(int variant, int mode, bool tma, const ScanParams& p,
-                               const TmaMaps& maps, unsigned blocks, cudaStream_t stream,
-                               bool pdl);
+// exp_mode: how the exact variants form exp (ExpMode of scan_device.cuh:
+// 0 SFU, 1 CUDA expf, 2 the reference backend's exp); ignored otherwise.
+cudaError_t launch_scan_kernel(int variant, int exp_mode, int mode, bool tma,
+                               const ScanParams& p, const TmaMaps& maps, unsigned blocks,
+                               cudaStream_t stream, bool pdl);
 
 // Enqueue the carry kernel (between the aggregate and emit passes of a split
 // plan), as a programmatic dependent launch.
@@ -67,7 +69,7 @@ cudaError_t launch_carry_kernel(const ScanParams& p, cudaStream_t stream);
 cudaError_t launch_wait_selftest(uint64_t limit_ns, cudaStream_t stream);
 
 // Resident CTAs per SM of one kernel instantiation (occupancy calculator).
-cudaError_t max_blocks_per_sm(int variant, int mode, bool tma, int* blocks);
+cudaError_t max_blocks_per_sm(int variant, int exp_mode, int mode, bool tma, int* blocks);
 
 // Record `msg` as the calling thread's mamba_scan_last_error(); returns status.
 int set_last_error(int status, const std::string& msg);

@@ -19,6 +19,11 @@ OPS = {
     "SelectiveScanFusedExact": 3,
 }
 FUSED = {"SelectiveScanFused", "SelectiveScanFusedExact"}
+EXACT = {"SelectiveScanExact", "SelectiveScanFusedExact"}
+# How the Exact ops form exp (include/mamba_scan.h, MAMBA_SCAN_EXP_*): None =
+# the SFU's ex2.approx; "ieee" = CUDA's expf; "reference" = the reference C++
+# backend's own polynomial exp, to follow that backend's numbers.
+EXP_FLAGS = {None: 0, "ieee": 0x100, "reference": 0x200}
 
 STATUS_OK = 0
 
@@ -126,12 +131,24 @@ def _check(name, t, shape):
         raise ValueError(f"{name} must have shape {tuple(shape)}, got {tuple(t.shape)}")
 
 
-def workspace_size(op: str, batch: int, dim: int, seqlen: int, dstate: int = 16) -> int:
-    return int(library().mamba_scan_workspace_size(OPS[op], batch, dim, seqlen, dstate))
+def _variant(op: str, exp) -> int:
+    if op not in OPS:
+        raise ValueError(f"unknown op {op!r}")
+    if exp not in EXP_FLAGS:
+        raise ValueError(f"exp must be one of {list(EXP_FLAGS)}, got {exp!r}")
+    if exp is not None and op not in EXACT:
+        raise ValueError(f"exp={exp!r} applies to the Exact ops only, not {op}")
+    return OPS[op] | EXP_FLAGS[exp]
+
+
+def workspace_size(op: str, batch: int, dim: int, seqlen: int, dstate: int = 16,
+                   exp=None) -> int:
+    return int(library().mamba_scan_workspace_size(_variant(op, exp), batch, dim, seqlen,
+                                                   dstate))
 
 
 def selective_scan(op: str, u, delta, A, B, C, D, z=None, *, delta_bias=None, h0=None,
-                   out=None, h_last=None, workspace=None, chunked=True, stream=None):
+                   out=None, h_last=None, workspace=None, chunked=True, stream=None, exp=None):
     """Run one selective-scan op on CUDA tensors; returns ``out`` ([batch, dim, seqlen]).
 
     op: one of the four reference op names. Layouts: u/delta/z [B,D,L], A [D,N],
@@ -140,11 +157,12 @@ def selective_scan(op: str, u, delta, A, B, C, D, z=None, *, delta_bias=None, h0
     workspace_size(...) bytes is taken from torch's allocator.
     chunked: False passes no workspace, so the sequence runs as one pass.
     stream: a torch.cuda.Stream (default: the current stream).
+    exp: Exact ops only: None (SFU exp), "ieee" (CUDA's expf) or "reference"
+    (the reference C++ backend's polynomial exp; see EXP_FLAGS).
     """
     import torch
 
-    if op not in OPS:
-        raise ValueError(f"unknown op {op!r}")
+    code = _variant(op, exp)
     if u.dim() != 3 or A.dim() != 2:
         raise ValueError("u must be [batch, dim, seqlen] and A [dim, dstate]")
     batch, dim, seqlen = u.shape
@@ -162,7 +180,7 @@ def selective_scan(op: str, u, delta, A, B, C, D, z=None, *, delta_bias=None, h0
     else:
         _check("out", out, (batch, dim, seqlen))
     lib = library()
-    ws_bytes = int(lib.mamba_scan_workspace_size(OPS[op], batch, dim, seqlen, dstate))
+    ws_bytes = int(lib.mamba_scan_workspace_size(code, batch, dim, seqlen, dstate))
     if not chunked:
         workspace = None
     elif workspace is None and ws_bytes > 0:
@@ -171,7 +189,7 @@ def selective_scan(op: str, u, delta, A, B, C, D, z=None, *, delta_bias=None, h0
                     _ptr(z) if op in FUSED else None, _ptr(delta_bias), _ptr(h0), _ptr(out),
                     _ptr(h_last), batch, dim, seqlen, dstate)
     st = stream if stream is not None else torch.cuda.current_stream(u.device)
-    rc = lib.mamba_scan_launch(OPS[op], ctypes.byref(args), _ptr(workspace),
+    rc = lib.mamba_scan_launch(code, ctypes.byref(args), _ptr(workspace),
                                0 if workspace is None else workspace.numel(), st.cuda_stream)
     if rc != STATUS_OK:
         raise ScanError(rc, f"{op}: {lib.mamba_scan_status_string(rc).decode()}: "

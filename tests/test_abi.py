@@ -68,6 +68,10 @@ def _args(**kw):
     (dict(seqlen=-1), 0, 1, "negative"),
     (dict(u=None), 1, 1, "non-NULL"),
     (dict(z=None), 2, 1, "need z"),
+    (dict(), 0 | 0x200, 1, "exact variants only"),   # exp flag on a linear op
+    (dict(), 2 | 0x100, 1, "exact variants only"),
+    (dict(), 1 | 0x300, 1, "at most one"),            # two exp flags
+    (dict(), 1 | 0x400, 1, "variant"),                # unknown flag
 ])
 def test_launch_rejects_bad_arguments_before_any_cuda_call(kw, variant, status, msg):
     lib = cuda.library()
@@ -324,3 +328,12 @@ def test_workspace_plan():
     assert cuda.workspace_size("SelectiveScanFused", 8, 5120, 2048) == 96 * 32 * 5 * 32 * 4
     # few row tiles, long sequence: everything is split
     assert cuda.workspace_size("SelectiveScanExact", 1, 2048, 16384) > 0
+
+
+def test_python_binding_checks_exp_modes():
+    assert cuda._variant("SelectiveScanExact", "reference") == 1 | 0x200
+    assert cuda._variant("SelectiveScanFusedExact", "ieee") == 3 | 0x100
+    with pytest.raises(ValueError, match="Exact ops only"):
+        cuda._variant("SelectiveScanFused", "ieee")
+    with pytest.raises(ValueError, match="exp must be"):
+        cuda._variant("SelectiveScanExact", "fast")

@@ -32,7 +32,7 @@ def _inputs(batch, dim, seqlen, device):
     return u, delta, A, B, C, D, z
 
 
-def _worker(rank, world, port, batch, dim, seqlen, q):
+def _worker(rank, world, port, batch, dim, seqlen, chunked, q):
     import torch.distributed as dist
     from datetime import timedelta
 
@@ -48,10 +48,11 @@ def _worker(rank, world, port, batch, dim, seqlen, q):
         inputs = _inputs(batch, dim, seqlen, dev)  # every rank builds the same global tensors
         plan = shard_plan(batch, dim, world, rank)
         local = plan.slice_inputs(*inputs)
-        out_local = cuda.selective_scan("SelectiveScanFused", *local[:7], delta_bias=local[7])
+        out_local = cuda.selective_scan("SelectiveScanFused", *local[:7], delta_bias=local[7],
+                                        chunked=chunked)
         full = gather_output(out_local, plan)
         if rank == 0:
-            ref = cuda.selective_scan("SelectiveScanFused", *inputs)
+            ref = cuda.selective_scan("SelectiveScanFused", *inputs, chunked=chunked)
             q.put(("ok", float((full - ref).abs().max().item()), tuple(full.shape)))
         dist.barrier()
     except Exception as e:  # noqa: BLE001
@@ -61,8 +62,11 @@ def _worker(rank, world, port, batch, dim, seqlen, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("batch,dim,seqlen", [(4, 256, 512), (1, 300, 256)])
-def test_sharded_scan_gathered_on_rank0(batch, dim, seqlen):
+# The unchunked case (batch 16: 8 per rank) runs every row as one pass on both
+# sides, so the bits agree whatever sequence split either shape would plan.
+@pytest.mark.parametrize("batch,dim,seqlen,chunked", [(4, 256, 512, True), (1, 300, 256, True),
+                                                      (16, 512, 1024, False)])
+def test_sharded_scan_gathered_on_rank0(batch, dim, seqlen, chunked):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
@@ -70,7 +74,7 @@ def test_sharded_scan_gathered_on_rank0(batch, dim, seqlen):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, batch, dim, seqlen, q))
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, batch, dim, seqlen, chunked, q))
              for r in range(2)]
     for p in procs:
         p.start()

@@ -211,6 +211,18 @@ def test_config_8x5120x2048_fused_rows():
     check_rows("SelectiveScanFused", inputs, out)
 
 
+def test_config_64x5120x4096_fused_rows():
+    """The multi-GPU configuration's whole batch (64 x 5120 x 4096, 21.5 GB of
+    tensors) on one GPU: 48 sampled rows against the float64 oracle, the
+    first and last row among them."""
+    inputs = gpu_config(64, 5120, 4096, True, seed=3)
+    out = cuda.selective_scan("SelectiveScanFused", *inputs)
+    assert torch.isfinite(out).all()
+    check_rows("SelectiveScanFused", inputs, out)
+    del inputs, out
+    torch.cuda.empty_cache()
+
+
 def test_config_1x2048x16384_exact_rows_and_chunking():
     inputs = gpu_config(1, 2048, 16384, False, seed=2, exact_dt_per_element=True)
     out = cuda.selective_scan("SelectiveScanExact", *inputs[:6])
