@@ -700,6 +700,20 @@ def run_model(args):
     scan_ms = timed(sgraph.replay, 20)
     launches_per_scan = 3 if cuda.workspace_size(SCAN_OP, B, D, L) > 0 else 1
 
+    # the same forward run eagerly, its 24 scans through the ONNX Runtime
+    # custom-op entry (CreateKernelV2 once per op, KernelComputeV2 per call)
+    # on the CUDA-EP host of tests/fake_ort, as an ORT session would run them
+    sys.path.insert(0, str(ROOT / "tests"))
+    from fake_ort import ort_shim
+
+    ort_scan = ort_shim.OrtScan()
+    x_ids = ids.clone()
+    for _ in range(2):
+        model(x_ids, scan=ort_scan)
+    torch.cuda.synchronize()
+    ort_ms = max_over_ranks(timed(lambda: model(x_ids, scan=ort_scan), max(3, args.e2e_steps)))
+    ort_scan.close()
+
     if rank == 0:
         hbm_peak, peak_kind = measured_peaks()
         algo = model.cfg.n_layer * algorithmic_bytes(B, D, L)
@@ -723,6 +737,11 @@ def run_model(args):
             # GEMM
             "gpu_launches": (model.cfg.n_layer * (7 + launches_per_scan) + 3) * args.steps,
             "scan_ms_per_step": scan_ms,
+            "ort_entry": {"ms_per_step": ort_ms, "value": world * B * L / (ort_ms * 1e-3),
+                          "unit": MODEL_UNIT,
+                          "path": "eager forward (no CUDA graph), every scan through "
+                                  "RegisterCustomOps -> CreateKernelV2 -> KernelComputeV2 on "
+                                  "the tests/fake_ort CUDA-EP host"},
             "roofline": {"bound": "hbm", "kernel": f"the {model.cfg.n_layer} {SCAN_OP} calls of "
                          f"one forward (1x{D}x{L} each)", "achieved": achieved, "peak": hbm_peak,
                          "unit": "GB/s", "frac": achieved / hbm_peak, "traffic": None,

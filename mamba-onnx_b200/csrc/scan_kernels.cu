@@ -638,7 +638,9 @@ __global__ void __launch_bounds__(kRows, MAMBA_SCAN_MIN_BLOCKS)
       fence_mbarrier_init();
     }
     __syncwarp();
+    int issued = 0;  // tiles whose loads lane 0 has issued
     auto issue = [&](int k, int s) {
+      ++issued;
       const int t0 = (int)(l_begin + (int64_t)k * kT);
       mbar_arrive_expect_tx(&sm.full[s], kStageBytes);
       tma_load_3d(sm.u[s], &maps.u, &sm.full[s], t0, d0, b);
@@ -654,7 +656,17 @@ __global__ void __launch_bounds__(kRows, MAMBA_SCAN_MIN_BLOCKS)
       const int s = k % kStages;
       const bool ok = mbar_wait(&sm.full[s], (uint32_t)(k / kStages) & 1u, &g_scan_device_error);
       if (!__all_sync(0xffffffffu, ok)) {  // timeout recorded; all lanes leave together
-        if (M == kEmit && lane == 0) bulk_wait_all<0>();  // no store may still read smem
+        if (lane == 0) {
+          // Before the CTA's shared memory can go to another CTA: give the
+          // loads already issued for later tiles up to 100 ms each to land
+          // (a lost one never will; its wait gives up too), and let no
+          // store still read shared memory.
+          for (int j = k + 1; j < issued; ++j)
+            mbar_wait(&sm.full[j % kStages], (uint32_t)(j / kStages) & 1u, &g_scan_device_error,
+                      100000000ull);
+          if (M == kEmit) bulk_wait_all<0>();
+        }
+        __syncwarp();
         return;
       }
       const int64_t t0 = l_begin + (int64_t)k * kT;

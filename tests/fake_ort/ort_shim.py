@@ -237,3 +237,52 @@ class InferenceSession:
         self.run_device(dev, out, st)
         st.synchronize()
         return [out.cpu().numpy()]
+
+
+class OrtScan:
+    """A drop-in for mamba_onnx.cuda.selective_scan that runs every call
+    through the library's ONNX Runtime custom-op entry (one session per op
+    name: RegisterCustomOps, CreateKernelV2 once, KernelComputeV2 per call)
+    on the caller's stream, as ORT's CUDA EP would run a graph's scan nodes.
+
+    Pass it as ``scan=`` to mamba_onnx.model (MambaLM.forward). The op has
+    the reference's inputs plus the optional delta_bias; it has no state
+    input or output, so h0 / h_last must be None.
+    """
+
+    def __init__(self, library_path=None):
+        import mamba_onnx
+
+        self.opts = SessionOptions()
+        if library_path is None:
+            mamba_onnx.register_custom_ops(self.opts, backend="cuda")
+        else:
+            self.opts.register_custom_ops_library(str(library_path))
+        self.sessions = {}
+
+    def session(self, op, with_bias):
+        key = (op, with_bias)
+        if key not in self.sessions:
+            fused = "Fused" in op
+            self.sessions[key] = InferenceSession(make_model(op, fused, with_delta_bias=with_bias),
+                                                  self.opts, providers=["CUDAExecutionProvider"])
+        return self.sessions[key]
+
+    def __call__(self, op, u, delta, A, B, C, D, z=None, *, delta_bias=None, h0=None,
+                 out=None, h_last=None, stream=None, **_):
+        import torch
+
+        if h0 is not None or h_last is not None:
+            raise ValueError("the ONNX Runtime op has no state input or output")
+        fused = "Fused" in op
+        with_bias = fused and delta_bias is not None
+        inputs = [u, delta, A, B, C, D] + ([z] if fused else []) + ([delta_bias] if with_bias else [])
+        if out is None:
+            out = torch.empty(u.shape, dtype=torch.float32, device=u.device)
+        return self.session(op, with_bias).run_device(
+            [t.contiguous() for t in inputs], out, stream)
+
+    def close(self):
+        for s in self.sessions.values():
+            s.close()
+        self.sessions.clear()

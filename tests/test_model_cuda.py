@@ -115,3 +115,29 @@ def test_captured_decode_step_equals_eager(cuda_device):
         eager = model.step(ids[:, t], state)
         torch.cuda.synchronize()
         assert torch.equal(g_logits, eager), t
+
+
+def test_forward_with_scans_through_the_ort_op_entry(cuda_device):
+    """The 130m forward with each of its 24 scans run through the library's
+    ONNX Runtime custom-op entry (RegisterCustomOps, CreateKernelV2,
+    KernelComputeV2 on the CUDA-EP host of tests/fake_ort, with dt_proj.bias
+    as the op's optional delta_bias input) gives the same logits, bit for bit,
+    as the forward calling the C ABI directly: the op layer adds nothing to
+    the numbers. The 1x1536x1024 scans take the chunked path, so the kernel's
+    per-stream scratch is exercised too."""
+    import sys
+    from pathlib import Path
+
+    sys.path.insert(0, str(Path(__file__).resolve().parent))
+    from fake_ort import ort_shim
+
+    model = MambaLM(mamba_130m()).init_random(seed=2).to(cuda_device)
+    x = _ids(model.cfg.vocab_size, 1024, 7, cuda_device)
+    scan = ort_shim.OrtScan()
+    try:
+        via_op = model(x, scan=scan)
+        direct = model(x)
+        torch.cuda.synchronize()
+        assert torch.equal(via_op, direct)
+    finally:
+        scan.close()
