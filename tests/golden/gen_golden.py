@@ -1,6 +1,6 @@
 """Generate the golden vectors under tests/golden/ (run where the reference tree exists).
 
-    python tests/golden/gen_golden.py [--reference /root/reference]
+    python tests/golden/gen_golden.py --reference <path of the reference checkout>
 
 For every case of the reference's own test suite (tests/test_ops.py) this
 records the input recipe (rebuilt by tests/scan_cases.py), a sha256 of the
@@ -99,7 +99,9 @@ def sc_flags(op):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True,
+                    help="root of the acmiyaguchi/mamba-onnx checkout whose tests/test_ops.py "
+                         "and compiled plugin (oracle/_ref) produce the vectors")
     args = ap.parse_args()
     ref_fn = load_reference_fn(Path(args.reference))
     manifest = {}
