@@ -954,6 +954,7 @@ def run_decode(args):
     import torch
     import torch.distributed as dist
 
+    from mamba_onnx import model as M
     from mamba_onnx.model import MambaLM, mamba_130m
 
     torch.cuda.set_device(local)
@@ -1022,10 +1023,14 @@ def run_decode(args):
                     "h2d_bytes_per_step": host_ids.numel() * 8,
                     "d2h_bytes_per_step": host_next.numel() * 8, "ms_per_step": e2e_ms,
                     "path": "pinned token ids -> graph replay -> argmax token to host"},
-            # this package's kernels per token: per block RMSNorm + in_proj,
-            # the convolution step, x_proj, the fused dt_proj + scan step and
-            # out_proj + residual; then the final RMSNorm + LM head
-            "gpu_launches": (model.cfg.n_layer * 5 + 1) * args.steps,
+            # this package's kernels per token: the persistent decoding kernel
+            # (every block and the LM head in one launch), or per block
+            # RMSNorm + in_proj, the convolution step, x_proj, the fused
+            # dt_proj + scan step and out_proj + residual, then the final
+            # RMSNorm + LM head
+            "gpu_launches": (1 if M.DECODE == "persistent" else model.cfg.n_layer * 5 + 1)
+                            * args.steps,
+            "decode": M.DECODE,
             "clocks": clocks.summary()}), flush=True)
     if world > 1:
         del graph

@@ -122,6 +122,90 @@ MAMBA_SCAN_API int mamba_x_proj(const float* x, const float* weight, float* dt, 
                                 int64_t dstate, void* stream);
 
 /*
+ * mamba_x_proj with Mamba's dt_proj fused behind it (its bias left to the
+ * scan op's delta_bias input, which adds it before softplus):
+ *   delta[b, d, t] = sum_{k < rank} dt_weight[d, k] * dt[b, t, k]
+ * where dt is the first `rank` outputs of x_proj, which are not written out;
+ * B and C as mamba_x_proj writes them. x [batch][dim][seqlen], weight
+ * [rank + 2*dstate][dim], dt_weight [dim][rank], delta [batch][dim][seqlen]
+ * (the scan op's layout), B and C [batch][seqlen][dstate]. rank <= 96 and
+ * rank + 2*dstate <= 128; fp32, deterministic (dt summed as mamba_x_proj
+ * does, then delta in k order). No output may overlap an input or another
+ * output.
+ */
+MAMBA_SCAN_API int mamba_x_proj_delta(const float* x, const float* weight, const float* dt_weight,
+                                      float* delta, float* B, float* C, int64_t batch,
+                                      int64_t dim, int64_t seqlen, int64_t rank, int64_t dstate,
+                                      void* stream);
+
+/*
+ * Mamba's dt_proj for every token, without its bias (the scan op adds it
+ * through its delta_bias input before softplus):
+ *   delta[b, d, t] = sum_{k < rank} weight[d, k] * dt[b, t, k]
+ * dt is x_proj's [batch][seqlen][rank] output, weight dt_proj's [dim][rank],
+ * delta [batch][dim][seqlen] (the scan op's layout), not overlapping either
+ * input. fp32, summed in k order (deterministic).
+ */
+MAMBA_SCAN_API int mamba_dt_proj(const float* dt, const float* weight, float* delta,
+                                 int64_t batch, int64_t dim, int64_t seqlen, int64_t rank,
+                                 void* stream);
+
+/*
+ * One Mamba block's weights and decoding state for mamba_decode_step (device
+ * pointers; fp32, contiguous): norm_weight [d_model], in_proj_weight
+ * [2*d_inner][d_model], conv_weight [d_inner][d_conv], conv_bias [d_inner] or
+ * NULL, x_proj_weight [rank + 2*dstate][d_inner], dt_proj_weight
+ * [d_inner][rank], dt_proj_bias [d_inner] or NULL, A [d_inner][dstate]
+ * (= -exp(A_log)), D [d_inner], out_proj_weight [d_model][d_inner]
+ * (in_proj_weight and out_proj_weight 16-byte aligned);
+ * conv_state [batch][d_inner][d_conv] (last inputs, oldest first) and
+ * ssm_state [batch][d_inner][dstate], both updated in place.
+ */
+typedef struct mamba_decode_layer {
+  const float* norm_weight;
+  const float* in_proj_weight;
+  const float* conv_weight;
+  const float* conv_bias;
+  const float* x_proj_weight;
+  const float* dt_proj_weight;
+  const float* dt_proj_bias;
+  const float* A;
+  const float* D;
+  const float* out_proj_weight;
+  float* conv_state;
+  float* ssm_state;
+} mamba_decode_layer;
+
+/* Bytes of scratch mamba_decode_step needs (0 for a bad shape). */
+MAMBA_SCAN_API size_t mamba_decode_scratch_size(int64_t batch, int64_t d_inner, int64_t rank,
+                                                int64_t dstate);
+
+/*
+ * One decoding step of a whole Mamba model in one persistent kernel:
+ * for each of the n_layer blocks (layers: a DEVICE array of n_layer
+ * mamba_decode_layer), h += out_proj(SSM step(x_proj(conv step(in_proj(
+ * RMSNorm(h)))))) exactly as mamba_rmsnorm_gemv, mamba_causal_conv1d_step,
+ * mamba_x_proj, mamba_ssm_decode_step and mamba_gemv compute it (the same
+ * values, bit for bit), then logits = lm_head . RMSNorm(h; norm_f_weight).
+ * h [batch][d_model] is the residual stream after the embedding (updated in
+ * place), lm_head [vocab][d_model] (16-byte aligned), logits [batch][vocab].
+ * scratch: mamba_decode_scratch_size() bytes, 16-byte aligned, not
+ * overlapping any other argument; its first 128 bytes (the barrier counter) are zeroed on `stream`
+ * before the launch. batch 1..4, dstate 16, d_conv 1..8, rank 1..256,
+ * d_model and d_inner multiples of 4, batch * max(d_model, d_inner) <= 40960.
+ * A cooperative launch of one CTA per SM; its grid-wide barriers give up
+ * after 2 s and report MAMBA_SCAN_ERR_DEVICE_TIMEOUT through
+ * mamba_scan_check_device_error(). Calls on the same scratch must not
+ * overlap on the GPU.
+ */
+MAMBA_SCAN_API int mamba_decode_step(const mamba_decode_layer* layers, int64_t n_layer, float* h,
+                                     const float* norm_f_weight, const float* lm_head,
+                                     float* logits, void* scratch, size_t scratch_bytes,
+                                     int64_t batch, int64_t d_model, int64_t d_inner,
+                                     int64_t d_conv, int64_t rank, int64_t dstate, int64_t vocab,
+                                     float eps, void* stream);
+
+/*
  * Split fp32 values into two tf32 parts for mamba_gemm_tf32x3:
  *   hi = tf32(x), lo = tf32(x - hi)   (round to nearest; x - hi is exact),
  * written as [rows][cols] with row stride `ld` (>= cols) into hi and lo.

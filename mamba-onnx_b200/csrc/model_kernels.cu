@@ -341,17 +341,29 @@ union XpSmem {
   XpStage stage;
   float part[kXpTokens][kXpRow];  // this CTA's partial sums, [t][j]
 };
-constexpr size_t kXpSmemBytes = sizeof(XpSmem);
+// x_proj with dt_proj fused (kDelta): up to this dt_rank. After the partial
+// sums are added, the union holds dt of the cluster's 32 tokens as [k][t]
+// (row stride 33) and then a chunk of dt_proj's weight as [k][96 d].
+constexpr int kXpDtMaxRank = 96;
+constexpr int kXpDtRow = kXpTokens + 1;
+static_assert(kXpDtMaxRank * (kXpDtRow + kXpDChunk) * 4 <= sizeof(XpSmem), "fused dt_proj smem");
+// ... plus, outside the union, this CTA's 4 finished token rows of dt, [k][4]
+constexpr size_t kXpDtlBytes = (size_t)kXpMaxOut * (kXpTokens / kXpCluster) * 4;
+constexpr size_t kXpSmemBytes = sizeof(XpSmem) + kXpDtlBytes;
 
 // kOut = outputs per thread (P <= 32 kOut): 3 for Mamba-130m's P = 80.
-template <int kOut>
-__global__ void __cluster_dims__(kXpCluster, 1, 1) __launch_bounds__(kXpThreads)
+// kDelta: dt_proj fused, delta[b, d, t] = sum_k w_dt[d, k] dt[b, t, k]
+// written instead of dt (rank <= kXpDtMaxRank): each CTA of the cluster
+// forms delta for its own d_inner range and the cluster's 32 tokens.
+template <int kOut, bool kDelta>
+__global__ void __cluster_dims__(kXpCluster, 1, 1) __launch_bounds__(kXpThreads, 2)
     xproj_kernel(const float* __restrict__ x, const float* __restrict__ w, float* __restrict__ dt,
                  float* __restrict__ Bm, float* __restrict__ Cm, int dim, int seqlen, int rank,
-                 int dstate) {
+                 int dstate, const float* __restrict__ w_dt, float* __restrict__ delta) {
   pdl_enter();
   extern __shared__ __align__(16) uint8_t xp_raw[];
   XpSmem& sm = *reinterpret_cast<XpSmem*>(xp_raw);
+  float* dtl = reinterpret_cast<float*>(xp_raw + sizeof(XpSmem));  // kDelta: [k][4]
   cg::cluster_group cluster = cg::this_cluster();
   const int crank = (int)cluster.block_rank();
   const int b = blockIdx.y;
@@ -368,17 +380,34 @@ __global__ void __cluster_dims__(kXpCluster, 1, 1) __launch_bounds__(kXpThreads)
 #pragma unroll
     for (int k = 0; k < kOut; ++k) acc[a][k] = 0.f;
 
-  for (int dc = d_lo; dc < d_hi; dc += kXpDChunk) {
-    __syncthreads();  // the previous chunk has been read
-    for (int i = tid; i < kXpDChunk * kXpTokens; i += kXpThreads) {
-      const int dd = i / kXpTokens, tt = i % kXpTokens;
-      const int d = dc + dd, t = t0 + tt;
-      sm.stage.x[dd][tt] = (d < d_hi && t < seqlen) ? __ldg(xb + (int64_t)d * seqlen + t) : 0.f;
+  // Loads of a 96-row chunk go to registers first, all issued before any is
+  // stored (x: 12 per thread, rows of 32 tokens; W: 12 kOut per thread, rows
+  // of 96 d_inner values, zeros for the unused columns P..32 kOut): one
+  // load round trip per chunk.
+  constexpr int kXq = kXpDChunk * kXpTokens / kXpThreads;       // 12
+  constexpr int kWq = kXpDChunk * 32 * kOut / kXpThreads;       // 12 kOut
+  float xr[kXq], wr[kWq];
+  auto fetch = [&](int dc) {
+#pragma unroll
+    for (int q = 0; q < kXq; ++q) {
+      const int d = dc + (tid >> 5) + 8 * q, t = t0 + (tid & 31);
+      xr[q] = (d < d_hi && t < seqlen) ? __ldg(xb + (int64_t)d * seqlen + t) : 0.f;
     }
-    for (int i = tid; i < P * kXpDChunk; i += kXpThreads) {
-      const int j = i / kXpDChunk, dd = i % kXpDChunk;
-      const int d = dc + dd;
-      sm.stage.w[dd][j] = (d < d_hi) ? __ldg(w + (int64_t)j * dim + d) : 0.f;
+#pragma unroll
+    for (int q = 0; q < kWq; ++q) {
+      const int i = tid + kXpThreads * q, j = i / kXpDChunk, d = dc + i % kXpDChunk;
+      wr[q] = (j < P && d < d_hi) ? __ldg(w + (int64_t)j * dim + d) : 0.f;
+    }
+  };
+  for (int dc = d_lo; dc < d_hi; dc += kXpDChunk) {
+    fetch(dc);
+    __syncthreads();  // the previous chunk has been read
+#pragma unroll
+    for (int q = 0; q < kXq; ++q) sm.stage.x[(tid >> 5) + 8 * q][tid & 31] = xr[q];
+#pragma unroll
+    for (int q = 0; q < kWq; ++q) {
+      const int i = tid + kXpThreads * q;
+      sm.stage.w[i % kXpDChunk][i / kXpDChunk] = wr[q];
     }
     __syncthreads();
     const int n = min(kXpDChunk, d_hi - dc);
@@ -387,7 +416,7 @@ __global__ void __cluster_dims__(kXpCluster, 1, 1) __launch_bounds__(kXpThreads)
       const float4 xv = *reinterpret_cast<const float4*>(&sm.stage.x[dd][4 * tg]);
 #pragma unroll
       for (int k = 0; k < kOut; ++k) {
-        const float wv = sm.stage.w[dd][og + 32 * k];  // columns >= P: unused sums
+        const float wv = sm.stage.w[dd][og + 32 * k];  // columns >= P: zeros, unused sums
         acc[0][k] = fmaf(xv.x, wv, acc[0][k]);
         acc[1][k] = fmaf(xv.y, wv, acc[1][k]);
         acc[2][k] = fmaf(xv.z, wv, acc[2][k]);
@@ -413,14 +442,73 @@ __global__ void __cluster_dims__(kXpCluster, 1, 1) __launch_bounds__(kXpThreads)
 #pragma unroll
     for (int r = 0; r < kXpCluster; ++r) sum += parts[r][tt * kXpRow + j];
     const int t = t0 + tt;
+    if (kDelta && j < rank) dtl[j * kRows + (tt - crank * kRows)] = sum;
     if (t < seqlen) {
       const int64_t row = (int64_t)b * seqlen + t;
-      if (j < rank)
-        dt[row * rank + j] = sum;
-      else if (j < rank + dstate)
+      if (j < rank) {
+        if (!kDelta) dt[row * rank + j] = sum;
+      } else if (j < rank + dstate) {
         Bm[row * dstate + (j - rank)] = sum;
-      else
+      } else {
         Cm[row * dstate + (j - rank - dstate)] = sum;
+      }
+    }
+  }
+  if constexpr (kDelta) {
+    // every CTA's 4 rows of dt are final, and no CTA reads the partial tiles
+    // any more: the union is free
+    cluster.sync();
+    float* dtf = &sm.part[0][0];                 // dt of the 32 tokens, [k][t]
+    float* wdt = dtf + kXpDtMaxRank * kXpDtRow;  // w_dt of 96 d_inner rows, [k][d]
+    for (int i = tid; i < kXpTokens * rank; i += kXpThreads) {
+      const int k = i / kXpTokens, tt = i % kXpTokens;
+      const float* src = cluster.map_shared_rank(dtl, tt / kRows);
+      dtf[k * kXpDtRow + tt] = src[k * kRows + tt % kRows];
+    }
+    const int warp = tid >> 5, lane = tid & 31;  // lane = token, warp = 12 rows of the chunk
+    constexpr int kWq = kXpDtMaxRank * kXpDChunk / kXpThreads;  // 36 loads per thread
+    for (int dc = d_lo; dc < d_hi; dc += kXpDChunk) {
+      float r[kWq];
+#pragma unroll
+      for (int q = 0; q < kWq; ++q) {
+        const int i = tid + kXpThreads * q, dd = i % kXpDChunk, k = i / kXpDChunk;
+        r[q] = (k < rank && dc + dd < d_hi) ? __ldg(w_dt + (int64_t)(dc + dd) * rank + k) : 0.f;
+      }
+      __syncthreads();  // dtf is complete; the previous chunk's weights have been read
+#pragma unroll
+      for (int q = 0; q < kWq; ++q) {
+        const int i = tid + kXpThreads * q;
+        wdt[(i / kXpDChunk) * kXpDChunk + i % kXpDChunk] = r[q];
+      }
+      __syncthreads();
+      float2 a2[6];
+#pragma unroll
+      for (int i = 0; i < 6; ++i) a2[i] = make_float2(0.f, 0.f);
+      const float* wrow = wdt + 12 * warp;
+#pragma unroll 4
+      for (int k = 0; k < rank; ++k) {
+        const float dv = dtf[k * kXpDtRow + lane];
+        const float2 d2 = make_float2(dv, dv);
+        const float4 w0 = *reinterpret_cast<const float4*>(wrow + k * kXpDChunk);
+        const float4 w1 = *reinterpret_cast<const float4*>(wrow + k * kXpDChunk + 4);
+        const float4 w2 = *reinterpret_cast<const float4*>(wrow + k * kXpDChunk + 8);
+        a2[0] = mamba_scan::fma2(make_float2(w0.x, w0.y), d2, a2[0]);
+        a2[1] = mamba_scan::fma2(make_float2(w0.z, w0.w), d2, a2[1]);
+        a2[2] = mamba_scan::fma2(make_float2(w1.x, w1.y), d2, a2[2]);
+        a2[3] = mamba_scan::fma2(make_float2(w1.z, w1.w), d2, a2[3]);
+        a2[4] = mamba_scan::fma2(make_float2(w2.x, w2.y), d2, a2[4]);
+        a2[5] = mamba_scan::fma2(make_float2(w2.z, w2.w), d2, a2[5]);
+      }
+      const int t = t0 + lane;
+      if (t < seqlen) {
+#pragma unroll
+        for (int i = 0; i < 6; ++i) {
+          const int d = dc + 12 * warp + 2 * i;
+          float* o = delta + ((int64_t)b * dim + d) * seqlen + t;
+          if (d < d_hi) o[0] = a2[i].x;
+          if (d + 1 < d_hi) o[seqlen] = a2[i].y;
+        }
+      }
     }
   }
   cluster.sync();  // no CTA leaves while another still reads its shared memory
@@ -480,16 +568,23 @@ __global__ void __launch_bounds__(256)
 
 template <int kOut>
 cudaError_t launch_xproj(dim3 grid, cudaStream_t st, const float* x, const float* w, float* dt,
-                         float* Bm, float* Cm, int dim, int seqlen, int rank, int dstate) {
+                         float* Bm, float* Cm, int dim, int seqlen, int rank, int dstate,
+                         const float* w_dt = nullptr, float* delta = nullptr) {
   static std::once_flag once;
   static cudaError_t attr = cudaSuccess;
   std::call_once(once, [] {
-    attr = cudaFuncSetAttribute(xproj_kernel<kOut>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)kXpSmemBytes);
+    attr = cudaFuncSetAttribute(xproj_kernel<kOut, false>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kXpSmemBytes);
+    if (attr == cudaSuccess)
+      attr = cudaFuncSetAttribute(xproj_kernel<kOut, true>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kXpSmemBytes);
   });
   if (attr != cudaSuccess) return attr;
-  return launch_pdl(xproj_kernel<kOut>, grid, dim3(kXpThreads), kXpSmemBytes, st, x, w, dt, Bm, Cm,
-                    dim, seqlen, rank, dstate);
+  if (delta != nullptr)
+    return launch_pdl(xproj_kernel<kOut, true>, grid, dim3(kXpThreads), kXpSmemBytes, st, x, w,
+                      dt, Bm, Cm, dim, seqlen, rank, dstate, w_dt, delta);
+  return launch_pdl(xproj_kernel<kOut, false>, grid, dim3(kXpThreads), kXpSmemBytes, st, x, w, dt,
+                    Bm, Cm, dim, seqlen, rank, dstate, w_dt, delta);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -497,6 +592,97 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 bool overlap(const void* a, size_t abytes, const void* b, size_t bbytes) {
   const auto a0 = reinterpret_cast<uintptr_t>(a), b0 = reinterpret_cast<uintptr_t>(b);
   return a0 < b0 + bbytes && b0 < a0 + abytes;
+}
+
+// ----------------------------------------------------------------- dt_proj
+
+// delta[b, d, l] = sum_k W[d, k] * dt[b, l, k]: the block's dt_proj (its bias
+// is added inside the scan op, through delta_bias), written as the [B, D, L]
+// delta the scan reads. A GEMM with K = dt_rank (48 for Mamba-130m), far too
+// shallow for tensor-core tiles to pay. One CTA of 128 threads per 64 (d) x
+// 64 (l) tile (Mamba-130m: 384 CTAs, all resident at once), K in steps of up
+// to 64 held whole in shared memory, stored k-major so that each thread
+// reads its 4 d and 8 l values as float4s; each thread keeps 4 x 8 outputs
+// (packed FFMA2 over l pairs) summed in k order, and stores float4 runs
+// along l. The weight tile is loaded before waiting for the previous kernel.
+constexpr int kDtBM = 64, kDtBN = 64, kDtBK = 64, kDtThreads = 128;
+
+__global__ void __launch_bounds__(kDtThreads)
+    dt_proj_kernel(const float* __restrict__ dt, const float* __restrict__ w,
+                   float* __restrict__ delta, int dim, int seqlen, int rank) {
+  __shared__ __align__(16) float ws[kDtBK][kDtBM];
+  __shared__ __align__(16) float xs[kDtBK][kDtBN + 4];
+  const int tid = threadIdx.x;
+  const int b = blockIdx.z, d0 = blockIdx.y * kDtBM, l0 = blockIdx.x * kDtBN;
+  const float* dtb = dt + (int64_t)b * seqlen * rank;
+  const int ty = tid >> 3, tx = tid & 7;  // outputs: d0 + 4ty + i, l0 + 4tx + {0..3, 32..35}
+  float2 acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = make_float2(0.f, 0.f);
+  // Loader roles: element i = tid + 128 j of a 64 x kn tile is (row i % 64,
+  // k = i / 64); every load of a tile is issued before any is stored.
+  constexpr int kLd = kDtBM * kDtBK / kDtThreads;  // 32 elements per thread and tile
+  const int lrow = tid & 63, lk = tid >> 6;
+  float r[kLd];
+  for (int k0 = 0; k0 < rank; k0 += kDtBK) {
+    const int kn = min(kDtBK, rank - k0);
+    if (k0 > 0) __syncthreads();  // the previous K step has been read
+#pragma unroll
+    for (int j = 0; j < kLd; ++j) {
+      const int k = lk + 2 * j;
+      r[j] = (d0 + lrow < dim && k < kn) ? __ldg(w + (int64_t)(d0 + lrow) * rank + k0 + k) : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < kLd; ++j) ws[lk + 2 * j][lrow] = r[j];
+    // dt is the previous kernel's output (x_proj): wait for it (a no-op
+    // unless launched as a programmatic dependent launch)
+    if (k0 == 0) pdl_enter();
+#pragma unroll
+    for (int j = 0; j < kLd; ++j) {
+      const int k = lk + 2 * j;
+      r[j] = (l0 + lrow < seqlen && k < kn) ? dtb[(int64_t)(l0 + lrow) * rank + k0 + k] : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < kLd; ++j) xs[lk + 2 * j][lrow] = r[j];
+    __syncthreads();
+#pragma unroll 8
+    for (int k = 0; k < kn; ++k) {
+      const float4 wv = *reinterpret_cast<const float4*>(&ws[k][4 * ty]);
+      const float4 x0 = *reinterpret_cast<const float4*>(&xs[k][4 * tx]);
+      const float4 x1 = *reinterpret_cast<const float4*>(&xs[k][32 + 4 * tx]);
+      const float wi[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 w2 = make_float2(wi[i], wi[i]);
+        acc[i][0] = mamba_scan::fma2(w2, make_float2(x0.x, x0.y), acc[i][0]);
+        acc[i][1] = mamba_scan::fma2(w2, make_float2(x0.z, x0.w), acc[i][1]);
+        acc[i][2] = mamba_scan::fma2(w2, make_float2(x1.x, x1.y), acc[i][2]);
+        acc[i][3] = mamba_scan::fma2(w2, make_float2(x1.z, x1.w), acc[i][3]);
+      }
+    }
+  }
+  const bool vec = (seqlen & 3) == 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int d = d0 + 4 * ty + i;
+    if (d >= dim) break;
+    float* row = delta + ((int64_t)b * dim + d) * seqlen;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int l = l0 + 32 * h + 4 * tx;
+      const float2 a = acc[i][2 * h], c = acc[i][2 * h + 1];
+      if (vec && l + 3 < seqlen) {
+        *reinterpret_cast<float4*>(row + l) = make_float4(a.x, a.y, c.x, c.y);
+      } else {
+        const float v[4] = {a.x, a.y, c.x, c.y};
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (l + j < seqlen) row[l + j] = v[j];
+      }
+    }
+  }
 }
 
 }  // namespace
@@ -610,6 +796,69 @@ int mamba_x_proj(const float* x, const float* weight, float* dt, float* B, float
                             (int)dstate)
           : launch_xproj<4>(grid, st, x, weight, dt, B, C, (int)dim, (int)seqlen, (int)rank,
                             (int)dstate);
+  if (e != cudaSuccess) return set_last_error(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
+  return MAMBA_SCAN_OK;
+}
+
+int mamba_x_proj_delta(const float* x, const float* weight, const float* dt_weight, float* delta,
+                       float* B, float* C, int64_t batch, int64_t dim, int64_t seqlen,
+                       int64_t rank, int64_t dstate, void* stream) {
+  using mamba_scan::set_last_error;
+  if (batch < 0 || dim < 0 || seqlen < 0 || rank < 1 || dstate < 1 || rank > kXpDtMaxRank ||
+      rank + 2 * dstate > kXpMaxOut)
+    return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT,
+                          "x_proj_delta: bad shape (rank 1.." + std::to_string(kXpDtMaxRank) +
+                              ", rank + 2 * dstate <= " + std::to_string(kXpMaxOut) + ")");
+  if (batch == 0 || seqlen == 0 || dim == 0) return MAMBA_SCAN_OK;
+  if (!x || !weight || !dt_weight || !delta || !B || !C)
+    return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "x_proj_delta: NULL pointer");
+  if (batch > 65535 || dim > ((int64_t)1 << 30) || seqlen > ((int64_t)1 << 30) ||
+      (seqlen + kXpTokens - 1) / kXpTokens * kXpCluster > 0x7FFFFFFF)
+    return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "x_proj_delta: too large");
+  const size_t xb = (size_t)(batch * dim * seqlen) * 4, wb = (size_t)((rank + 2 * dstate) * dim) * 4;
+  const size_t wdb = (size_t)(dim * rank) * 4, bcb = (size_t)(batch * seqlen * dstate) * 4;
+  const void* outs[3] = {delta, B, C};
+  const size_t out_bytes[3] = {xb, bcb, bcb};
+  for (int i = 0; i < 3; ++i) {
+    if (overlap(outs[i], out_bytes[i], x, xb) || overlap(outs[i], out_bytes[i], weight, wb) ||
+        overlap(outs[i], out_bytes[i], dt_weight, wdb))
+      return set_last_error(MAMBA_SCAN_ERR_ALIASING, "x_proj_delta: an output overlaps an input");
+    for (int k = i + 1; k < 3; ++k)
+      if (overlap(outs[i], out_bytes[i], outs[k], out_bytes[k]))
+        return set_last_error(MAMBA_SCAN_ERR_ALIASING, "x_proj_delta: outputs overlap");
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const dim3 grid((unsigned)((seqlen + kXpTokens - 1) / kXpTokens * kXpCluster), (unsigned)batch);
+  const cudaError_t e =
+      (rank + 2 * dstate <= 32 * 3)
+          ? launch_xproj<3>(grid, st, x, weight, nullptr, B, C, (int)dim, (int)seqlen, (int)rank,
+                            (int)dstate, dt_weight, delta)
+          : launch_xproj<4>(grid, st, x, weight, nullptr, B, C, (int)dim, (int)seqlen, (int)rank,
+                            (int)dstate, dt_weight, delta);
+  if (e != cudaSuccess) return set_last_error(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
+  return MAMBA_SCAN_OK;
+}
+
+int mamba_dt_proj(const float* dt, const float* weight, float* delta, int64_t batch, int64_t dim,
+                  int64_t seqlen, int64_t rank, void* stream) {
+  using mamba_scan::set_last_error;
+  if (batch < 0 || dim < 0 || seqlen < 0 || rank < 1)
+    return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "dt_proj: bad shape");
+  if (batch == 0 || dim == 0 || seqlen == 0) return MAMBA_SCAN_OK;
+  if (!dt || !weight || !delta)
+    return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "dt_proj: NULL pointer");
+  if (batch > 65535 || dim > ((int64_t)1 << 30) || seqlen > ((int64_t)1 << 30) ||
+      rank > ((int64_t)1 << 20) || (dim + kDtBM - 1) / kDtBM > 65535)
+    return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "dt_proj: too large");
+  const size_t db = (size_t)(batch * dim * seqlen) * 4;
+  if (overlap(delta, db, dt, (size_t)(batch * seqlen * rank) * 4) ||
+      overlap(delta, db, weight, (size_t)(dim * rank) * 4))
+    return set_last_error(MAMBA_SCAN_ERR_ALIASING, "dt_proj: delta overlaps an input");
+  const dim3 grid((unsigned)((seqlen + kDtBN - 1) / kDtBN), (unsigned)((dim + kDtBM - 1) / kDtBM),
+                  (unsigned)batch);
+  dt_proj_kernel<<<grid, kDtThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      dt, weight, delta, (int)dim, (int)seqlen, (int)rank);
+  const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_last_error(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
   return MAMBA_SCAN_OK;
 }

@@ -368,7 +368,10 @@ int mamba_scan_check_device_error(void) {
   // the model-ops GEMM keeps its own word (same codes)
   const int g = mamba_gemm::read_and_clear_error();
   if (g < 0) return fail(MAMBA_SCAN_ERR_CUDA, "cannot read the GEMM error word");
-  return code != 0 ? code : g;
+  // and so does the persistent decoding kernel
+  const int dc = mamba_decode::read_and_clear_error();
+  if (dc < 0) return fail(MAMBA_SCAN_ERR_CUDA, "cannot read the decode error word");
+  return code != 0 ? code : (g != 0 ? g : dc);
 }
 
 int mamba_scan_selftest_wait_timeout(int64_t limit_ns, void* stream) {

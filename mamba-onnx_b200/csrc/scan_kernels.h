@@ -101,6 +101,12 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
 
 }  // namespace mamba_scan
 
+namespace mamba_decode {
+// The persistent decoding kernel's error word (a barrier wait that gave up):
+// its code, or -1 when it cannot be read; cleared when set.
+int read_and_clear_error();
+}  // namespace mamba_decode
+
 namespace mamba_gemm {
 // The tensor-core GEMM's own error word (a bounded wait that gave up): its
 // code, or -1 when it cannot be read; cleared when set.

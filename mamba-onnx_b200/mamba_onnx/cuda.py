@@ -98,6 +98,18 @@ def library() -> ctypes.CDLL:
             [ctypes.c_void_p] * 9 + [ctypes.c_int64] * 4 + [ctypes.c_void_p]
         lib.mamba_x_proj.restype = ctypes.c_int
         lib.mamba_x_proj.argtypes = [ctypes.c_void_p] * 5 + [ctypes.c_int64] * 5 + [ctypes.c_void_p]
+        lib.mamba_decode_scratch_size.restype = ctypes.c_size_t
+        lib.mamba_decode_scratch_size.argtypes = [ctypes.c_int64] * 4
+        lib.mamba_decode_step.restype = ctypes.c_int
+        lib.mamba_decode_step.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
+                                          ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                          ctypes.c_void_p, ctypes.c_size_t] + \
+            [ctypes.c_int64] * 7 + [ctypes.c_float, ctypes.c_void_p]
+        lib.mamba_x_proj_delta.restype = ctypes.c_int
+        lib.mamba_x_proj_delta.argtypes = [ctypes.c_void_p] * 6 + [ctypes.c_int64] * 5 + \
+            [ctypes.c_void_p]
+        lib.mamba_dt_proj.restype = ctypes.c_int
+        lib.mamba_dt_proj.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int64] * 4 + [ctypes.c_void_p]
         lib.mamba_split_tf32.restype = ctypes.c_int
         lib.mamba_split_tf32.argtypes = [ctypes.c_void_p] + [ctypes.c_int64] * 3 + \
             [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p]
@@ -400,6 +412,119 @@ def x_proj(x, weight, rank: int, dstate: int, stream=None):
     if rc != STATUS_OK:
         _raise(rc, "x_proj")
     return dt, Bm, Cm
+
+
+DECODE_LAYER_FIELDS = ("norm_weight", "in_proj_weight", "conv_weight", "conv_bias",
+                       "x_proj_weight", "dt_proj_weight", "dt_proj_bias", "A", "D",
+                       "out_proj_weight", "conv_state", "ssm_state")
+
+
+def decode_layer_table(layers, device):
+    """The DEVICE array of struct mamba_decode_layer (include/mamba_model_ops.h)
+    for mamba_decode_step: ``layers`` is a list of dicts mapping each name of
+    DECODE_LAYER_FIELDS to a contiguous CUDA float32 tensor (conv_bias and
+    dt_proj_bias may be None). Returns an int64 tensor of the pointers; the
+    tensors must outlive it."""
+    import torch
+
+    rows = []
+    for lay in layers:
+        row = []
+        for f in DECODE_LAYER_FIELDS:
+            t = lay.get(f)
+            if t is None and f not in ("conv_bias", "dt_proj_bias"):
+                raise ValueError(f"decode layer needs {f}")
+            if t is not None and (not t.is_cuda or t.dtype != torch.float32
+                                  or not t.is_contiguous()):
+                raise TypeError(f"{f} must be a contiguous CUDA float32 tensor")
+            if f in ("in_proj_weight", "out_proj_weight") and t.data_ptr() % 16:
+                raise ValueError(f"{f} must be 16-byte aligned")
+            row.append(0 if t is None else t.data_ptr())
+        rows.append(row)
+    return torch.tensor(rows, dtype=torch.int64).to(device)
+
+
+def decode_scratch_size(batch: int, d_inner: int, rank: int, dstate: int = 16) -> int:
+    return int(library().mamba_decode_scratch_size(batch, d_inner, rank, dstate))
+
+
+def decode_step(table, n_layer: int, h, norm_f_weight, lm_head, logits, scratch, *, d_inner: int,
+                d_conv: int, rank: int, dstate: int, eps: float, stream=None):
+    """One decoding step of the whole model in one persistent kernel
+    (mamba_decode_step): h [B, d_model] (the embedded tokens; becomes the
+    final residual stream), logits [B, vocab] written; the layers' states in
+    ``table`` (decode_layer_table) advance by one token. scratch: a uint8
+    CUDA tensor of decode_scratch_size(...) bytes, used by one call at a time."""
+    batch, d_model = h.shape
+    vocab = lm_head.shape[0]
+    _check("h", h, (batch, d_model))
+    _check("norm_f_weight", norm_f_weight, (d_model,))
+    _check("lm_head", lm_head, (vocab, d_model))
+    _check("logits", logits, (batch, vocab))
+    import torch
+
+    st = stream if stream is not None else torch.cuda.current_stream(h.device)
+    rc = library().mamba_decode_step(_ptr(table), n_layer, _ptr(h), _ptr(norm_f_weight),
+                                     _ptr(lm_head), _ptr(logits), _ptr(scratch), scratch.numel(),
+                                     batch, d_model, d_inner, d_conv, rank, dstate, vocab,
+                                     float(eps), st.cuda_stream)
+    if rc != STATUS_OK:
+        _raise(rc, "decode_step")
+    return logits
+
+
+X_PROJ_DELTA_MAX_RANK = 96
+
+
+def x_proj_delta(x, weight, dt_weight, rank: int, dstate: int, stream=None):
+    """x_proj with dt_proj fused behind it: x [B, D, L] (contiguous CUDA
+    float32), weight [rank + 2*dstate, D], dt_weight [D, rank] (rank <= 96).
+    Returns (delta [B, D, L], B [B, L, dstate], C [B, L, dstate]) with
+    delta[b, d, t] = sum_k dt_weight[d, k] * dt[b, t, k], dt being x_proj's
+    first rank outputs (dt_proj's bias is not added)."""
+    import torch
+
+    if x.dim() != 3:
+        raise ValueError("x must be [batch, dim, seqlen]")
+    batch, dim, seqlen = x.shape
+    _check("x", x, (batch, dim, seqlen))
+    _check("weight", weight, (rank + 2 * dstate, dim))
+    _check("dt_weight", dt_weight, (dim, rank))
+    kw = dict(dtype=torch.float32, device=x.device)
+    delta = torch.empty(batch, dim, seqlen, **kw)
+    Bm = torch.empty(batch, seqlen, dstate, **kw)
+    Cm = torch.empty(batch, seqlen, dstate, **kw)
+    st = stream if stream is not None else torch.cuda.current_stream(x.device)
+    rc = library().mamba_x_proj_delta(_ptr(x), _ptr(weight), _ptr(dt_weight), _ptr(delta),
+                                      _ptr(Bm), _ptr(Cm), batch, dim, seqlen, rank, dstate,
+                                      st.cuda_stream)
+    if rc != STATUS_OK:
+        _raise(rc, "x_proj_delta")
+    return delta, Bm, Cm
+
+
+def dt_proj(dt, weight, out=None, stream=None):
+    """Mamba's dt_proj without its bias: dt [B, L, rank] (x_proj's output,
+    contiguous CUDA float32), weight [D, rank] -> delta [B, D, L] with
+    delta[b, d, t] = sum_k weight[d, k] * dt[b, t, k] (the scan op's layout)."""
+    import torch
+
+    if dt.dim() != 3 or weight.dim() != 2:
+        raise ValueError("dt must be [batch, seqlen, rank] and weight [dim, rank]")
+    batch, seqlen, rank = dt.shape
+    dim = weight.shape[0]
+    _check("dt", dt, (batch, seqlen, rank))
+    _check("weight", weight, (dim, rank))
+    if out is None:
+        out = torch.empty(batch, dim, seqlen, dtype=torch.float32, device=dt.device)
+    else:
+        _check("out", out, (batch, dim, seqlen))
+    st = stream if stream is not None else torch.cuda.current_stream(dt.device)
+    rc = library().mamba_dt_proj(_ptr(dt), _ptr(weight), _ptr(out), batch, dim, seqlen, rank,
+                                 st.cuda_stream)
+    if rc != STATUS_OK:
+        _raise(rc, "dt_proj")
+    return out
 
 
 class SplitTF32:

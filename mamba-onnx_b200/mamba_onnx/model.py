@@ -18,9 +18,11 @@ fp32 accumulation: fp32-accurate; ``GEMM = "cublas"`` selects torch's fp32
 GEMMs instead); single-token steps use torch's fp32 GEMMs for those
 projections. x_proj, whose 80-wide output is too narrow to fill the GPU with
 GEMM tiles, runs on this package's fp32 kernel (d_inner split over a cluster
-of 8 CTAs, or one warp per output when decoding; dt, B and C written apart);
-dt_proj stays on torch's fp32 GEMM, which measured faster than a kernel of
-ours. ``forward`` runs a whole sequence; ``step`` decodes one
+of 8 CTAs, or one warp per output when decoding; dt, B and C written apart),
+and dt_proj runs fused behind it (each CTA of the cluster forms the scan's
+[B, D, L] delta for its own d_inner rows from the cluster's dt; ``DT_PROJ``
+selects a standalone kernel or torch's fp32 GEMM instead). ``forward`` runs a whole
+sequence; ``step`` decodes one
 token from a ``DecodeState`` (the convolution window and the 16 scan states
 per channel), which the scan carries in through ``h0`` and out through
 ``h_last``. On CUDA tensors the RMSNorms and the causal convolution + SiLU run
@@ -38,6 +40,13 @@ import torch.nn.functional as F
 from . import cuda
 
 SCAN_OP = "SelectiveScanFusedExact"
+# decoding on CUDA: one persistent kernel per token ("persistent"; batch <= 4,
+# d_model <= 1024, d_inner <= 2048, dt_rank <= 64, d_conv <= 4, else the
+# chain) or the chain of per-block kernels ("chain"); both give the same values
+DECODE = "persistent"
+# dt_proj on CUDA: fused behind x_proj ("fused", dt_rank <= 96; else "kernel"),
+# this package's standalone kernel ("kernel") or torch's fp32 GEMM ("cublas")
+DT_PROJ = "cublas"
 
 
 @dataclass(frozen=True)
@@ -157,10 +166,15 @@ class MambaLayer(torch.nn.Module):
         """x [B, D, L] after conv + SiLU -> delta [B, D, L] (before bias), B, C [B, L, N]."""
         N, R = self.cfg.d_state, self.cfg.rank
         if x.is_cuda:  # this package's x_proj: dt, B, C written apart, no copies
+            if DT_PROJ == "fused" and R <= cuda.X_PROJ_DELTA_MAX_RANK:
+                return cuda.x_proj_delta(x.contiguous(), self.x_proj_weight.detach(),
+                                         self.dt_proj_weight.detach(), R, N)
             dt, Bm, Cm = cuda.x_proj(x.contiguous(), self.x_proj_weight.detach(), R, N)
-            if x.shape[0] == 1:  # a 2-D GEMM on the transposed view writes [D, L] directly
-                return torch.mm(self.dt_proj_weight, dt[0].t()).unsqueeze(0), Bm, Cm
-            return torch.matmul(self.dt_proj_weight, dt.transpose(1, 2)), Bm, Cm  # [B, D, L]
+            if DT_PROJ == "cublas":
+                if x.shape[0] == 1:  # a 2-D GEMM on the transposed view writes [D, L] directly
+                    return torch.mm(self.dt_proj_weight, dt[0].t()).unsqueeze(0), Bm, Cm
+                return torch.matmul(self.dt_proj_weight, dt.transpose(1, 2)), Bm, Cm
+            return cuda.dt_proj(dt, self.dt_proj_weight.detach()), Bm, Cm  # [B, D, L]
         if x.shape[0] == 1:  # 2-D GEMMs take the transposed views without copies
             x_dbl = torch.mm(x[0].t(), self.x_proj_weight.t()).unsqueeze(0)  # [1, L, R + 2N]
             delta = torch.mm(self.dt_proj_weight, x_dbl[0, :, :R].t()).unsqueeze(0)
@@ -336,9 +350,48 @@ class MambaLM(torch.nn.Module):
             conv=[torch.zeros(batch, cfg.d_inner, cfg.d_conv, device=dev) for _ in self.layers],
             ssm=[torch.zeros(batch, cfg.d_inner, cfg.d_state, device=dev) for _ in self.layers])
 
+    def _decode_setup(self, state: DecodeState, batch: int):
+        """(table, scratch) of mamba_decode_step for this state, built once per
+        state and weight version (the table holds the tensors' addresses)."""
+        key = (batch, tuple(t.data_ptr() for t in state.conv + state.ssm),
+               tuple((p.data_ptr(), p._version) for p in self.parameters()))
+        cached = getattr(self, "_decode_cache", None)
+        if cached is None or cached[0] != key:
+            cfg = self.cfg
+            rows = []
+            for layer, cs, ss in zip(self.layers, state.conv, state.ssm):
+                rows.append({
+                    "norm_weight": layer.norm_weight.detach(),
+                    "in_proj_weight": layer.in_proj_weight.detach(),
+                    "conv_weight": layer.conv_weight.detach(),
+                    "conv_bias": layer.conv_bias.detach(),
+                    "x_proj_weight": layer.x_proj_weight.detach(),
+                    "dt_proj_weight": layer.dt_proj_weight.detach(),
+                    "dt_proj_bias": layer.dt_proj_bias.detach(),
+                    "A": layer.A(), "D": layer.D.detach(),
+                    "out_proj_weight": layer.out_proj_weight.detach(),
+                    "conv_state": cs, "ssm_state": ss})
+            table = cuda.decode_layer_table(rows, self.embedding.device)
+            scratch = torch.empty(cuda.decode_scratch_size(batch, cfg.d_inner, cfg.rank,
+                                                           cfg.d_state),
+                                  dtype=torch.uint8, device=self.embedding.device)
+            self._decode_cache = (key, table, scratch, [r["A"] for r in rows])
+        return self._decode_cache[1], self._decode_cache[2]
+
     @torch.no_grad()
     def step(self, input_ids, state: DecodeState):
         """One decoding step: input_ids [B] -> logits [B, vocab]; state updated."""
+        cfg = self.cfg
+        if (input_ids.is_cuda and DECODE == "persistent" and input_ids.shape[0] <= 4
+                and cfg.d_model <= 1024 and cfg.d_inner <= 2048 and cfg.rank <= 64
+                and cfg.d_conv <= 4 and cfg.d_state == 16):
+            table, scratch = self._decode_setup(state, input_ids.shape[0])
+            h = F.embedding(input_ids, self.embedding)  # [B, d_model], becomes the last h
+            logits = torch.empty(input_ids.shape[0], cfg.vocab_size, device=h.device)
+            return cuda.decode_step(table, cfg.n_layer, h, self.norm_f_weight.detach(),
+                                    self.embedding.detach(), logits, scratch,
+                                    d_inner=cfg.d_inner, d_conv=cfg.d_conv, rank=cfg.rank,
+                                    dstate=cfg.d_state, eps=cfg.rms_eps)
         h = F.embedding(input_ids[:, None], self.embedding)
         for layer, cs, ss in zip(self.layers, state.conv, state.ssm):
             h = layer.step(h, layer.A(), cs, ss)

@@ -199,6 +199,57 @@ def test_x_proj_validates_before_launch():
     assert lib.mamba_x_proj(f, 2 * f, 3 * f, 4 * f, 5 * f, 0, 64, 16, 8, 16, None) == 0
 
 
+def test_dt_proj_validates_before_launch():
+    lib = cuda.library()
+    f = 0x100000
+    assert lib.mamba_dt_proj(f, 2 * f, 3 * f, 1, 64, 16, 0, None) == 1  # rank 0
+    assert lib.mamba_dt_proj(f, 2 * f, 3 * f, -1, 64, 16, 8, None) == 1
+    assert lib.mamba_dt_proj(None, 2 * f, 3 * f, 1, 64, 16, 8, None) == 1
+    assert lib.mamba_dt_proj(f, 2 * f, f + 64, 1, 64, 16, 8, None) == 4  # delta over dt
+    assert lib.mamba_dt_proj(f, 2 * f, 2 * f + 4, 1, 64, 16, 8, None) == 4  # delta over weight
+    assert lib.mamba_dt_proj(f, 2 * f, 3 * f, 0, 64, 16, 8, None) == 0  # empty: nothing to do
+    assert lib.mamba_dt_proj(f, 2 * f, 3 * f, 1, 64, 0, 8, None) == 0
+
+
+def test_x_proj_delta_validates_before_launch():
+    lib = cuda.library()
+    f = 0x100000
+    args = lambda **k: [k.get(n, v) for n, v in [  # noqa: E731
+        ("x", f), ("w", 2 * f), ("wdt", 3 * f), ("delta", 4 * f), ("B", 5 * f), ("C", 6 * f),
+        ("batch", 1), ("dim", 64), ("seqlen", 16), ("rank", 8), ("dstate", 16)]] + [None]
+    assert lib.mamba_x_proj_delta(*args(rank=97)) == 1  # dt_rank above 96
+    assert lib.mamba_x_proj_delta(*args(rank=80, dstate=40)) == 1  # rank + 2 dstate > 128
+    assert lib.mamba_x_proj_delta(*args(wdt=None)) == 1
+    assert lib.mamba_x_proj_delta(*args(delta=f + 64)) == 4  # delta over x
+    assert lib.mamba_x_proj_delta(*args(B=3 * f + 8)) == 4  # B over dt_weight
+    assert lib.mamba_x_proj_delta(*args(C=5 * f + 4)) == 4  # C over B
+    assert lib.mamba_x_proj_delta(*args(batch=0)) == 0
+
+
+def test_decode_step_validates_before_launch():
+    lib = cuda.library()
+    f = 0x100000
+    need = lib.mamba_decode_scratch_size(1, 1536, 48, 16)
+    assert need > 16 and lib.mamba_decode_scratch_size(0, 1536, 48, 16) == 0
+
+    def call(**k):
+        a = dict(layers=f, n=24, h=2 * f, nf=3 * f, lm=4 * f, logits=5 * f, scratch=6 * f,
+                 sbytes=need, batch=1, dm=768, di=1536, conv=4, rank=48, dstate=16,
+                 vocab=50280)
+        a.update(k)
+        return lib.mamba_decode_step(*a.values(), 1e-5, None)
+
+    assert call(batch=5) == 1          # at most 4 tokens
+    assert call(dstate=8) == 1
+    assert call(conv=9) == 1
+    assert call(dm=770) == 1           # d_model a multiple of 4
+    assert call(h=None) == 1
+    assert call(sbytes=need - 4) == 3  # scratch too small
+    assert call(scratch=6 * f + 8) == 3  # scratch misaligned
+    assert call(lm=4 * f + 4) == 1     # LM head misaligned
+    assert call(batch=4, dm=16384, sbytes=1 << 20) == 1  # shared-memory bound
+
+
 def test_empty_batch_is_a_no_op():
     lib = cuda.library()
     assert lib.mamba_scan_launch(0, ctypes.byref(_args(batch=0)), None, 0, None) == 0

@@ -117,6 +117,41 @@ def test_captured_decode_step_equals_eager(cuda_device):
         assert torch.equal(g_logits, eager), t
 
 
+@pytest.mark.parametrize("batch", [1, 3])
+def test_persistent_decode_equals_the_kernel_chain(cuda_device, batch):
+    """The one-kernel decoding step (mamba_decode_step: every block and the
+    LM head in one cooperative launch) against the chain of per-block
+    kernels from the same prefilled state: logits and both states equal bit
+    for bit over 6 tokens, eagerly and replayed as a CUDA graph."""
+    from mamba_onnx import cuda, model as M
+
+    model = MambaLM(mamba_130m()).init_random(seed=4).to(cuda_device)
+    ids = _ids(model.cfg.vocab_size, 40, 8, cuda_device, batch=batch)
+    _, state = model.prefill(ids[:, :32])
+    chain_state = model.new_state(batch)
+    model.copy_state(chain_state, state)
+    old = M.DECODE
+    try:
+        g_ids, g_logits, g_state, graph = model.capture_step(batch)
+        model.copy_state(g_state, state)
+        for t in range(32, 38):
+            M.DECODE = "chain"
+            ref = model.step(ids[:, t], chain_state)
+            M.DECODE = "persistent"
+            got = model.step(ids[:, t], state)
+            g_ids.copy_(ids[:, t])
+            graph.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(got, ref), t
+            assert torch.equal(g_logits, ref), t
+            for a, b, c in zip(state.conv + state.ssm, chain_state.conv + chain_state.ssm,
+                               g_state.conv + g_state.ssm):
+                assert torch.equal(a, b) and torch.equal(c, b), t
+    finally:
+        M.DECODE = old
+    assert cuda.check_device_error() == 0
+
+
 def test_forward_with_scans_through_the_ort_op_entry(cuda_device):
     """The 130m forward with each of its 24 scans run through the library's
     ONNX Runtime custom-op entry (RegisterCustomOps, CreateKernelV2,

@@ -114,6 +114,72 @@ def test_x_proj_matches_float64(batch, dim, seqlen, rank, dstate):
     assert cuda.check_device_error() == 0
 
 
+XPROJ_DELTA_CASES = [
+    (1, 1536, 1024, 48, 16),   # Mamba-130m
+    (2, 200, 77, 8, 16),       # ragged dim and seqlen
+    (3, 520, 130, 80, 16),     # P = 112: 4 outputs per thread
+    (1, 96, 5, 48, 16),        # five tokens: one cluster, mostly padding
+    (2, 2048, 64, 64, 16),     # dt_rank 64 (Mamba-370m widths)
+    (1, 300, 40, 96, 16),      # the largest dt_rank, P = 128
+]
+
+
+@pytest.mark.parametrize("batch,dim,seqlen,rank,dstate", XPROJ_DELTA_CASES)
+def test_x_proj_delta_equals_x_proj_then_dt_proj(batch, dim, seqlen, rank, dstate):
+    """x_proj with dt_proj fused behind it: delta within 2e-5 of the float64
+    chain's sum of magnitudes. Above 16 tokens, where mamba_x_proj takes the
+    same cluster kernel, B and C are bit-identical to mamba_x_proj's and
+    delta to mamba_dt_proj of mamba_x_proj's dt (same sums in the same order);
+    at 16 tokens or fewer mamba_x_proj sums in another order, and B and C are
+    compared with the float64 product instead."""
+    g = torch.Generator(device="cpu").manual_seed(batch * 13 + dim + rank)
+    x = torch.randn(batch, dim, seqlen, generator=g).cuda()
+    wx = (torch.randn(rank + 2 * dstate, dim, generator=g) * dim ** -0.5).cuda()
+    wdt = (torch.randn(dim, rank, generator=g) * rank ** -0.5).cuda()
+    delta, Bm, Cm = cuda.x_proj_delta(x, wx, wdt, rank, dstate)
+    dt, B2, C2 = cuda.x_proj(x, wx, rank, dstate)
+    if batch * seqlen > 16:
+        assert torch.equal(Bm, B2) and torch.equal(Cm, C2)
+        assert torch.equal(delta, cuda.dt_proj(dt, wdt))
+    else:
+        bc = torch.einsum("jd,bdt->btj", wx[rank:].double(), x.double())
+        bc_bound = torch.einsum("jd,bdt->btj", wx[rank:].double().abs(), x.double().abs())
+        got = torch.cat([Bm, Cm], dim=-1).double()
+        assert ((got - bc).abs() <= 1e-5 * bc_bound + 1e-30).all()
+    dt64 = torch.einsum("jd,bdt->btj", wx[:rank].double(), x.double())
+    ref = torch.einsum("dk,btk->bdt", wdt.double(), dt64)
+    bound = torch.einsum("dk,btk->bdt", wdt.double().abs(),
+                         torch.einsum("jd,bdt->btj", wx[:rank].double().abs(), x.double().abs()))
+    assert ((delta.double() - ref).abs() <= 2e-5 * bound + 1e-30).all()
+    assert cuda.check_device_error() == 0
+
+
+DTPROJ_CASES = [
+    (1, 1536, 1024, 48),   # Mamba-130m
+    (2, 5120, 300, 160),   # Mamba-2.8B widths, ragged seqlen (scalar tail stores)
+    (3, 70, 130, 7),       # dim and seqlen off the 64 x 128 tile, rank off the 16-step
+    (1, 64, 1, 48),        # one token
+]
+
+
+@pytest.mark.parametrize("batch,dim,seqlen,rank", DTPROJ_CASES)
+def test_dt_proj_matches_float64(batch, dim, seqlen, rank):
+    """dt_proj (delta[b, d, t] = sum_k W[d, k] dt[b, t, k]) against a float64
+    matmul of the same fp32 inputs: elementwise within 1e-5 of sum |W||dt|,
+    normwise 1e-6; repeated calls are bit-identical."""
+    g = torch.Generator(device="cpu").manual_seed(batch * 11 + dim + rank)
+    dt = torch.randn(batch, seqlen, rank, generator=g).cuda()
+    w = (torch.randn(dim, rank, generator=g) * rank ** -0.5).cuda()
+    delta = cuda.dt_proj(dt, w)
+    ref = torch.einsum("dk,btk->bdt", w.double(), dt.double())
+    bound = torch.einsum("dk,btk->bdt", w.double().abs(), dt.double().abs())
+    got = delta.double()
+    assert ((got - ref).abs() <= 1e-5 * bound + 1e-30).all()
+    assert float((got - ref).norm() / ref.norm()) < 1e-6
+    assert torch.equal(delta, cuda.dt_proj(dt, w))
+    assert cuda.check_device_error() == 0
+
+
 @pytest.mark.parametrize("batch,dim,width", [(1, 1536, 4), (3, 70, 4), (2, 33, 1), (2, 40, 8)])
 def test_conv1d_step_matches_torch_over_several_steps(batch, dim, width):
     """Decoding steps of the causal convolution: the window shifts in the new
