@@ -206,6 +206,18 @@ MAMBA_SCAN_API int mamba_decode_step(const mamba_decode_layer* layers, int64_t n
                                      float eps, void* stream);
 
 /*
+ * Self-test of mamba_decode_step's failure detection, without any fault:
+ * enqueues one CTA that arrives at a grid barrier which no other CTA joins,
+ * so its wait gives up after limit_ns (0 < limit_ns <= 10 s) exactly as a
+ * decoding step's barrier gives up after 2 s; a following
+ * mamba_scan_check_device_error() returns MAMBA_SCAN_ERR_DEVICE_TIMEOUT and
+ * the context stays usable. scratch: at least 128 bytes, 16-byte aligned
+ * (its first 128 bytes are zeroed first).
+ */
+MAMBA_SCAN_API int mamba_decode_selftest_barrier_timeout(int64_t limit_ns, void* scratch,
+                                                         size_t scratch_bytes, void* stream);
+
+/*
  * Split fp32 values into two tf32 parts for mamba_gemm_tf32x3:
  *   hi = tf32(x), lo = tf32(x - hi)   (round to nearest; x - hi is exact),
  * written as [rows][cols] with row stride `ld` (>= cols) into hi and lo.

@@ -114,7 +114,8 @@ __device__ __forceinline__ void barrier_arrive(unsigned int* ctl) {
 
 // Wait until every CTA has arrived at barrier k; false when the launch is
 // being abandoned (a wait timed out here or in another CTA).
-__device__ __noinline__ bool barrier_wait(unsigned int* ctl, unsigned int k) {
+__device__ __noinline__ bool barrier_wait(unsigned int* ctl, unsigned int k,
+                                          uint64_t limit_ns = kBarrierLimitNs) {
   __shared__ int ok_s;
   if (threadIdx.x == 0) {
     int ok = 1;
@@ -127,7 +128,7 @@ __device__ __noinline__ bool barrier_wait(unsigned int* ctl, unsigned int k) {
           ok = 0;
           break;
         }
-        if ((spins & 63u) == 63u && mamba_scan::globaltimer_ns() - start > kBarrierLimitNs) {
+        if ((spins & 63u) == 63u && mamba_scan::globaltimer_ns() - start > limit_ns) {
           atomicExch(ctl + 1, 1u);
           atomicExch(&g_decode_device_error, 6);  // MAMBA_SCAN_ERR_DEVICE_TIMEOUT
           ok = 0;
@@ -564,6 +565,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const Args a) {
   }
 }
 
+// The barrier's give-up path, without any fault: one CTA arrives at barrier
+// 2 (count 1 of the 2 it waits for), so its wait cannot complete and gives up
+// after limit_ns, recording the timeout.
+__global__ void __launch_bounds__(32) barrier_selftest_kernel(unsigned int* ctl, uint64_t limit_ns) {
+  barrier_arrive(ctl);
+  barrier_wait(ctl, 2, limit_ns);
+}
+
 }  // namespace
 
 int read_and_clear_error() {
@@ -589,6 +598,27 @@ size_t mamba_decode_scratch_size(int64_t batch, int64_t d_inner, int64_t rank, i
   // the barrier's control words, then x, z, y [batch][d_inner] and x_proj's outputs
   return 4 * (size_t)mamba_decode::kCtlWords +
          4 * (size_t)(3 * round_up4(batch * d_inner) + round_up4(batch * (rank + 2 * dstate)));
+}
+
+int mamba_decode_selftest_barrier_timeout(int64_t limit_ns, void* scratch, size_t scratch_bytes,
+                                          void* stream) {
+  using mamba_scan::set_last_error;
+  namespace md = mamba_decode;
+  if (limit_ns <= 0 || limit_ns > 10000000000LL)
+    return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "limit_ns must be in (0, 10 s]");
+  if (!scratch || scratch_bytes < 4 * (size_t)md::kCtlWords ||
+      (reinterpret_cast<uintptr_t>(scratch) & 15u) != 0)
+    return set_last_error(MAMBA_SCAN_ERR_WORKSPACE,
+                          "decode barrier self-test: scratch of at least 128 aligned bytes");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(scratch, 0, 4 * md::kCtlWords, st);
+  if (e == cudaSuccess) {
+    md::barrier_selftest_kernel<<<1, 32, 0, st>>>(static_cast<unsigned int*>(scratch),
+                                                  (uint64_t)limit_ns);
+    e = cudaGetLastError();
+  }
+  if (e != cudaSuccess) return set_last_error(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
+  return MAMBA_SCAN_OK;
 }
 
 int mamba_decode_step(const mamba_decode_layer* layers, int64_t n_layer, float* h,

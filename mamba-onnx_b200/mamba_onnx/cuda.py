@@ -105,6 +105,9 @@ def library() -> ctypes.CDLL:
                                           ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                           ctypes.c_void_p, ctypes.c_size_t] + \
             [ctypes.c_int64] * 7 + [ctypes.c_float, ctypes.c_void_p]
+        lib.mamba_decode_selftest_barrier_timeout.restype = ctypes.c_int
+        lib.mamba_decode_selftest_barrier_timeout.argtypes = [ctypes.c_int64, ctypes.c_void_p,
+                                                              ctypes.c_size_t, ctypes.c_void_p]
         lib.mamba_x_proj_delta.restype = ctypes.c_int
         lib.mamba_x_proj_delta.argtypes = [ctypes.c_void_p] * 6 + [ctypes.c_int64] * 5 + \
             [ctypes.c_void_p]
@@ -471,6 +474,18 @@ def decode_step(table, n_layer: int, h, norm_f_weight, lm_head, logits, scratch,
     if rc != STATUS_OK:
         _raise(rc, "decode_step")
     return logits
+
+
+def decode_selftest_barrier_timeout(limit_ns: int, scratch, stream=None) -> int:
+    """Enqueue the decoding kernel's barrier self-test (a grid barrier that
+    no other CTA joins, giving up after limit_ns); check_device_error() then
+    returns MAMBA_SCAN_ERR_DEVICE_TIMEOUT. scratch: a uint8 CUDA tensor of
+    at least 128 bytes. Returns the status."""
+    import torch
+
+    st = stream if stream is not None else torch.cuda.current_stream()
+    return int(library().mamba_decode_selftest_barrier_timeout(
+        int(limit_ns), _ptr(scratch), 0 if scratch is None else scratch.numel(), st.cuda_stream))
 
 
 X_PROJ_DELTA_MAX_RANK = 96

@@ -152,6 +152,31 @@ def test_persistent_decode_equals_the_kernel_chain(cuda_device, batch):
     assert cuda.check_device_error() == 0
 
 
+def test_decode_barrier_gives_up_and_the_context_survives(cuda_device):
+    """The decoding kernel's grid barrier bounded like its scan waits: a
+    barrier that no other CTA joins gives up after 20 ms and records
+    MAMBA_SCAN_ERR_DEVICE_TIMEOUT (no fault involved); a decoding step then
+    runs normally."""
+    import time
+
+    from mamba_onnx import cuda
+
+    scratch = torch.zeros(128, dtype=torch.uint8, device=cuda_device)
+    assert cuda.check_device_error() == 0
+    t0 = time.perf_counter()
+    assert cuda.decode_selftest_barrier_timeout(20_000_000, scratch) == 0
+    assert cuda.check_device_error() == 6
+    assert time.perf_counter() - t0 < 5.0
+    assert cuda.decode_selftest_barrier_timeout(0, scratch) == 1
+    assert cuda.decode_selftest_barrier_timeout(20_000_000, scratch[:64]) == 3
+    model = MambaLM(MambaConfig(d_model=64, n_layer=2, vocab_size=100)).init_random(seed=5)
+    model = model.to(cuda_device)
+    state = model.new_state(1)
+    logits = model.step(torch.tensor([3], device=cuda_device), state)
+    assert torch.isfinite(logits).all()
+    assert cuda.check_device_error() == 0
+
+
 def test_forward_with_scans_through_the_ort_op_entry(cuda_device):
     """The 130m forward with each of its 24 scans run through the library's
     ONNX Runtime custom-op entry (RegisterCustomOps, CreateKernelV2,
