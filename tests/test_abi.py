@@ -250,6 +250,18 @@ def test_decode_step_validates_before_launch():
     assert call(batch=4, dm=16384, sbytes=1 << 20) == 1  # shared-memory bound
 
 
+def test_decode_layer_table_checks_its_tensors():
+    import torch
+
+    good = {f: torch.zeros(4) for f in cuda.DECODE_LAYER_FIELDS}
+    with pytest.raises(TypeError, match="contiguous CUDA float32"):
+        cuda.decode_layer_table([good], "cpu")  # host tensors are refused
+    missing = dict(good)
+    del missing["A"]
+    with pytest.raises(ValueError, match="needs A"):
+        cuda.decode_layer_table([missing], "cpu")
+
+
 def test_empty_batch_is_a_no_op():
     lib = cuda.library()
     assert lib.mamba_scan_launch(0, ctypes.byref(_args(batch=0)), None, 0, None) == 0
