@@ -432,11 +432,12 @@ def decode_layer_table(layers, device):
 
     rows = []
     for lay in layers:
+        for f in DECODE_LAYER_FIELDS:
+            if lay.get(f) is None and f not in ("conv_bias", "dt_proj_bias"):
+                raise ValueError(f"decode layer needs {f}")
         row = []
         for f in DECODE_LAYER_FIELDS:
             t = lay.get(f)
-            if t is None and f not in ("conv_bias", "dt_proj_bias"):
-                raise ValueError(f"decode layer needs {f}")
             if t is not None and (not t.is_cuda or t.dtype != torch.float32
                                   or not t.is_contiguous()):
                 raise TypeError(f"{f} must be a contiguous CUDA float32 tensor")
