@@ -644,6 +644,19 @@ int mamba_decode_step(const mamba_decode_layer* layers, int64_t n_layer, float* 
                           "16-byte aligned");
   if ((reinterpret_cast<uintptr_t>(lm_head) & 15u) != 0)
     return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "decode_step: lm_head not 16-byte aligned");
+  {  // h, logits and scratch are written: pairwise disjoint, and apart from the LM head
+    const size_t hb = (size_t)(batch * d_model) * 4, lb = (size_t)(batch * vocab) * 4;
+    const size_t eb = (size_t)(vocab * d_model) * 4;
+    auto over = [](const void* x, size_t xb, const void* y, size_t yb) {
+      const auto x0 = reinterpret_cast<uintptr_t>(x), y0 = reinterpret_cast<uintptr_t>(y);
+      return x0 < y0 + yb && y0 < x0 + xb;
+    };
+    if (over(h, hb, logits, lb) || over(h, hb, scratch, scratch_bytes) ||
+        over(logits, lb, scratch, scratch_bytes) || over(lm_head, eb, h, hb) ||
+        over(lm_head, eb, logits, lb) || over(lm_head, eb, scratch, scratch_bytes))
+      return set_last_error(MAMBA_SCAN_ERR_ALIASING,
+                            "decode_step: h, logits, scratch and lm_head must not overlap");
+  }
   const size_t smem = sizeof(float) * (size_t)batch * (size_t)(d_model > d_inner ? d_model : d_inner);
   int dev = 0, sms = 0, coop = 0, per_sm = 0;
   cudaError_t e = cudaGetDevice(&dev);

@@ -233,7 +233,7 @@ def test_decode_step_validates_before_launch():
     assert need > 16 and lib.mamba_decode_scratch_size(0, 1536, 48, 16) == 0
 
     def call(**k):
-        a = dict(layers=f, n=24, h=2 * f, nf=3 * f, lm=4 * f, logits=5 * f, scratch=6 * f,
+        a = dict(layers=f, n=24, h=2 * f, nf=3 * f, lm=1 << 36, logits=5 * f, scratch=6 * f,
                  sbytes=need, batch=1, dm=768, di=1536, conv=4, rank=48, dstate=16,
                  vocab=50280)
         a.update(k)
@@ -246,8 +246,11 @@ def test_decode_step_validates_before_launch():
     assert call(h=None) == 1
     assert call(sbytes=need - 4) == 3  # scratch too small
     assert call(scratch=6 * f + 8) == 3  # scratch misaligned
-    assert call(lm=4 * f + 4) == 1     # LM head misaligned
-    assert call(batch=4, dm=16384, sbytes=1 << 20) == 1  # shared-memory bound
+    assert call(lm=(1 << 36) + 4) == 1  # LM head misaligned
+    assert call(batch=4, dm=16384, sbytes=1 << 20) == 1  # beyond the kernel's widths
+    assert call(logits=2 * f + 512) == 4  # logits inside h
+    assert call(scratch=5 * f + 64) == 4  # scratch inside logits
+    assert call(h=(1 << 36) + 4096) == 4  # h inside the LM head
 
 
 def test_decode_layer_table_checks_its_tensors():
