@@ -22,7 +22,10 @@
 // * 4, 8 or 12 accumulator warps (warp w owns TMEM lanes 32(w%4)..+31 = tile
 //   rows, and 64 columns) read each K block's sums (tcgen05.ld), add them to
 //   fp32 registers, then store C with arbitrary strides, optionally adding
-//   a second matrix C_in (which may be C itself).
+//   a second matrix C_in (which may be C itself): coalesced, through a
+//   shared-memory transpose when C is row-major (store_sums).
+// A second kernel computes 256 x BN tiles on CTA pairs (cta_group::2 MMAs,
+// gemm_tf32x3_pair_kernel); the host picks pairs or single CTAs per shape.
 // Every mbarrier wait is bounded (mamba_gemm error word on timeout).
 #include <cudaTypedefs.h>
 
@@ -90,6 +93,7 @@ struct Cfg {
   };
   static constexpr size_t kSmemBytes = sizeof(Smem) + 1024;  // + room to align the base
   static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
+  static constexpr size_t kStageBuffers = (size_t)kStages * kStageBytes;  // a_hi .. b_lo
 };
 using Cfg64 = Cfg<64, 4>;
 using Cfg128 = Cfg<128, 3>;
@@ -188,12 +192,85 @@ __device__ __forceinline__ void tmem_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// ---------------------------------------------------------------- epilogue
+
+// Floats of shared memory one accumulator warp uses to transpose its block
+// of sums (32 rows of kCols, one padding column: conflict-free both ways).
+template <int kCols>
+constexpr int kStoreScratch = 32 * (kCols + 1);
+
+// Writes one accumulator warp's block of sums to C: lane l holds the kCols
+// sums of row m_base + l, columns n_base... (acc[j/2].x / .y = column j),
+// C[m][n] = (C_in[m][n] +) sum. C_in may be C itself: every element is read
+// and written by the same thread, and each batch of reads is issued before
+// the batch's writes (C and C_in may alias, so the compiler cannot do it).
+// Column-major C (ldc_m == 1): the lanes' rows are consecutive addresses, so
+// each column is one coalesced store. Otherwise the block goes through
+// `scratch` (this warp's kStoreScratch<kCols> floats) and comes back one row
+// at a time, the lanes on consecutive columns.
+template <int kCols>
+__device__ __forceinline__ void store_sums(const GemmParams& p, const float2 (&acc)[kCols / 2],
+                                           int64_t m_base, int64_t n_base, float* scratch,
+                                           int lane) {
+  constexpr int kBatch = 16;
+  if (p.ldc_m == 1) {
+    const int64_t m = m_base + lane;
+    const bool m_ok = m < p.M;
+#pragma unroll
+    for (int j0 = 0; j0 < kCols; j0 += kBatch) {
+      float in[kBatch];
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j) {
+        const int64_t n = n_base + j0 + j;
+        in[j] = (p.c_in && m_ok && n < p.N) ? p.c_in[m + n * p.ldc_n] : 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j) {
+        const int64_t n = n_base + j0 + j;
+        const float a = ((j0 + j) & 1) ? acc[(j0 + j) / 2].y : acc[(j0 + j) / 2].x;
+        if (m_ok && n < p.N) p.c[m + n * p.ldc_n] = p.c_in ? in[j] + a : a;
+      }
+    }
+    return;
+  }
+  constexpr int kStride = kCols + 1, kPerRow = kCols / 32, kRows = kBatch / kPerRow;
+#pragma unroll
+  for (int j = 0; j < kCols; ++j)
+    scratch[lane * kStride + j] = (j & 1) ? acc[j / 2].y : acc[j / 2].x;
+  __syncwarp();
+#pragma unroll 1
+  for (int r0 = 0; r0 < 32; r0 += kRows) {
+    float v[kRows][kPerRow], in[kRows][kPerRow];
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) {
+      const int64_t m = m_base + r0 + r;
+#pragma unroll
+      for (int h = 0; h < kPerRow; ++h) {
+        const int64_t n = n_base + h * 32 + lane;
+        v[r][h] = scratch[(r0 + r) * kStride + h * 32 + lane];
+        in[r][h] = (p.c_in && m < p.M && n < p.N) ? p.c_in[m * p.ldc_m + n * p.ldc_n] : 0.f;
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) {
+      const int64_t m = m_base + r0 + r;
+#pragma unroll
+      for (int h = 0; h < kPerRow; ++h) {
+        const int64_t n = n_base + h * 32 + lane;
+        if (m < p.M && n < p.N) p.c[m * p.ldc_m + n * p.ldc_n] = p.c_in ? in[r][h] + v[r][h] : v[r][h];
+      }
+    }
+  }
+}
+
 // ------------------------------------------------------------------ kernel
 
 template <class C>
 __global__ void __launch_bounds__(C::kThreads, 1)
     gemm_tf32x3_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
   constexpr int BN = C::BN, kStages = C::kStages, kAccCols = C::kAccCols;
+  static_assert((size_t)C::kAccWarps * kStoreScratch<C::kAccCols> * 4 <= C::kStageBuffers,
+                "the store transposes fit in the stage buffers");
   constexpr int kProducerWarp = C::kProducerWarp, kMmaWarp = C::kMmaWarp;
   extern __shared__ uint8_t smem_raw[];
   typename C::Smem& sm = *reinterpret_cast<typename C::Smem*>(
@@ -321,24 +398,267 @@ __global__ void __launch_bounds__(C::kThreads, 1)
       tc_fence_before();
       mbar_arrive(&sm.acc_empty[b]);
     }
-    const int64_t m = (int64_t)m0 + quarter * 32 + lane;
-    if (__all_sync(0xffffffffu, ok) && m < p.M) {
-#pragma unroll
-      for (int j = 0; j < kAccCols; ++j) {
-        const int64_t n = (int64_t)n0 + col0 + j;
-        const float a = (j & 1) ? acc[j / 2].y : acc[j / 2].x;
-        if (n < p.N) {
-          const int64_t o = m * p.ldc_m + n * p.ldc_n;
-          p.c[o] = p.c_in ? p.c_in[o] + a : a;
-        }
-      }
-    }
+    // after the last block every stage has landed and been read by the
+    // MMAs: the stage buffers are free for the transposes of the stores
+    if (__all_sync(0xffffffffu, ok))
+      store_sums<kAccCols>(p, acc, (int64_t)m0 + quarter * 32, (int64_t)n0 + col0,
+                           reinterpret_cast<float*>(&sm) + warp * kStoreScratch<kAccCols>, lane);
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(C::kTmemCols)
+                 : "memory");
+  }
+}
+
+// ------------------------------------------------- CTA-pair (2-SM) kernel
+
+// The same GEMM on a pair of CTAs (a cluster of 2 on neighbouring SMs) that
+// computes one 256 x BN output tile with tcgen05.mma.cta_group::2: each CTA
+// holds 128 rows of the A tiles and half (BN/2 rows) of the B tiles, and the
+// tensor cores of the pair read both halves. Per K block a CTA streams
+// (2 * 128 + 2 * BN/2) x 128 bytes instead of (2 * 128 + 2 * BN) x 128 for
+// the same 128 x BN outputs of its own: the B tile crosses from L2 once per
+// pair. Each CTA loads its own halves by TMA (no multicast), completing on
+// the leader CTA's stage barrier; the leader's MMA warp issues the MMAs and
+// signals both CTAs' barriers (stage free, accumulator ready) at once; each
+// CTA drains its own 128 TMEM lanes (its 128 tile rows) and tells the
+// leader through its accumulator-free barrier. Every wait is bounded.
+template <int BN_, int kStages_>
+struct Cfg2 {
+  static constexpr int BN = BN_, kStages = kStages_;
+  static constexpr int kHalfN = BN / 2;  // B rows held by each CTA of the pair
+  static constexpr int kAccCols = 64;
+  static constexpr int kAccWarps = 4 * BN / kAccCols;
+  static constexpr int kAccThreads = 32 * kAccWarps;
+  static constexpr int kProducerWarp = kAccWarps, kMmaWarp = kAccWarps + 1;
+  static constexpr int kThreads = 32 * (kAccWarps + 2);
+  static constexpr uint32_t kATile = BM * BK * 4, kBTile = kHalfN * BK * 4;
+  static constexpr uint32_t kStageBytes = 2 * kATile + 2 * kBTile;  // one CTA's share
+  static constexpr int kTmemCols = (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
+  struct __align__(1024) Smem {
+    float a_hi[kStages][BM * BK];
+    float a_lo[kStages][BM * BK];
+    float b_hi[kStages][kHalfN * BK];
+    float b_lo[kStages][kHalfN * BK];
+    uint64_t full[kStages];   // leader: both CTAs' tiles of a stage have landed
+    uint64_t empty[kStages];  // each CTA: the pair's MMAs have read the stage
+    uint64_t acc_full[2];     // each CTA: a K block's sums are in TMEM buffer b
+    uint64_t acc_empty[2];    // leader: both CTAs' accumulator warps have read buffer b
+    uint32_t tmem_base;
+  };
+  static constexpr size_t kSmemBytes = sizeof(Smem) + 1024;
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
+  static constexpr size_t kStageBuffers = (size_t)kStages * kStageBytes;  // a_hi .. b_lo
+};
+using Cfg2x64 = Cfg2<64, 4>;
+using Cfg2x128 = Cfg2<128, 4>;
+using Cfg2x192 = Cfg2<192, 3>;
+using Cfg2x256 = Cfg2<256, 3>;
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// shared::cluster address of the same shared-memory location in CTA `rank`.
+__device__ __forceinline__ uint32_t map_to_rank(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
+               ::: "memory");
+}
+
+// 2-D TMA load into this CTA's shared memory, completing on the mbarrier at
+// shared::cluster address `bar` (the pair's leader).
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar,
+                                                 int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+// Instruction descriptor of kind::tf32 for the pair: M = 256.
+template <int BN>
+__device__ __forceinline__ void mma_tf32_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                              uint32_t accumulate) {
+  constexpr uint32_t kInstrDesc = (1u << 4) | (2u << 7) | (2u << 10) |
+                                  ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+  asm volatile(
+      "{\n\t"
+      ".reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t"
+      "}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(kInstrDesc), "r"(accumulate)
+      : "memory");
+}
+
+// One arrival on the barrier at the same offset in both CTAs of the pair
+// once the MMAs issued so far have completed.
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(smem_u32(bar)),
+      "h"((uint16_t)0x3)
+      : "memory");
+}
+
+// An arrival on a barrier of either CTA of the pair (CTA-scope release: the
+// waiting side orders TMEM accesses through tcgen05 fences, not through
+// this arrival, so no cluster-wide memory fence is needed).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+template <class C>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(C::kThreads, 1)
+    gemm_tf32x3_pair_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
+  constexpr int BN = C::BN, kStages = C::kStages, kAccCols = C::kAccCols;
+  static_assert((size_t)C::kAccWarps * kStoreScratch<C::kAccCols> * 4 <= C::kStageBuffers,
+                "the store transposes fit in the stage buffers");
+  constexpr int kProducerWarp = C::kProducerWarp, kMmaWarp = C::kMmaWarp;
+  extern __shared__ uint8_t smem_raw[];
+  typename C::Smem& sm = *reinterpret_cast<typename C::Smem*>(
+      smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();  // 0: the leader, which issues the MMAs
+  // pairs along M vary fastest; this CTA's A rows and B rows
+  const int m0 = (blockIdx.x >> 1) * 256 + (int)rank * BM;
+  const int n0 = blockIdx.y * BN;
+  const int nk = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mamba_scan::mbar_init(&sm.full[s], 1);
+      mamba_scan::mbar_init(&sm.empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mamba_scan::mbar_init(&sm.acc_full[b], 1);
+      mamba_scan::mbar_init(&sm.acc_empty[b], 2 * C::kAccWarps);
+    }
+    mamba_scan::fence_mbarrier_init();
+  }
+  if (warp == kProducerWarp && lane == 0) {
+    mamba_scan::prefetch_tensormap(&maps.a_hi);
+    mamba_scan::prefetch_tensormap(&maps.a_lo);
+    mamba_scan::prefetch_tensormap(&maps.b_hi);
+    mamba_scan::prefetch_tensormap(&maps.b_lo);
+  }
+  if (warp == 0) {  // the same warp of both CTAs allocates the pair's TMEM columns
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&sm.tmem_base)),
+                 "r"(C::kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  cluster_sync_all();  // both CTAs' barriers initialised, TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+  mamba_scan::pdl_trigger();
+  mamba_scan::pdl_wait();
+
+  if (warp == kProducerWarp) {
+    if (lane == 0) {
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % kStages;
+        if (kb >= kStages &&
+            !mamba_scan::mbar_wait(&sm.empty[s], (uint32_t)((kb / kStages) - 1) & 1u,
+                                   &g_gemm_device_error))
+          break;
+        // the leader's barrier counts both CTAs' bytes of the stage
+        if (rank == 0) mamba_scan::mbar_arrive_expect_tx(&sm.full[s], 2 * C::kStageBytes);
+        const uint32_t bar = map_to_rank(&sm.full[s], 0);
+        const int k0 = kb * BK;
+        tma_load_2d_pair(sm.a_hi[s], &maps.a_hi, bar, k0, m0);
+        tma_load_2d_pair(sm.a_lo[s], &maps.a_lo, bar, k0, m0);
+        tma_load_2d_pair(sm.b_hi[s], &maps.b_hi, bar, k0, n0 + (int)rank * C::kHalfN);
+        tma_load_2d_pair(sm.b_lo[s], &maps.b_lo, bar, k0, n0 + (int)rank * C::kHalfN);
+      }
+    }
+    __syncwarp();
+  } else if (warp == kMmaWarp) {
+    if (lane == 0 && rank == 0) {
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % kStages, b = kb & 1;
+        if (kb >= 2 && !mamba_scan::mbar_wait(&sm.acc_empty[b], (uint32_t)((kb >> 1) - 1) & 1u,
+                                              &g_gemm_device_error))
+          break;
+        if (!mamba_scan::mbar_wait(&sm.full[s], (uint32_t)(kb / kStages) & 1u,
+                                   &g_gemm_device_error))
+          break;
+        tc_fence_after();
+        const uint32_t t = tmem + (uint32_t)(b * BN);
+        const uint64_t ah = sw128_desc(sm.a_hi[s]), al = sw128_desc(sm.a_lo[s]);
+        const uint64_t bh = sw128_desc(sm.b_hi[s]), bl = sw128_desc(sm.b_lo[s]);
+#pragma unroll
+        for (int k = 0; k < BK / 8; ++k) {
+          const uint64_t off = (uint64_t)(k * 32) >> 4;
+          mma_tf32_pair<BN>(t, al + off, bh + off, k > 0 ? 1u : 0u);
+          mma_tf32_pair<BN>(t, ah + off, bl + off, 1u);
+        }
+#pragma unroll
+        for (int k = 0; k < BK / 8; ++k) {
+          const uint64_t off = (uint64_t)(k * 32) >> 4;
+          mma_tf32_pair<BN>(t, ah + off, bh + off, 1u);
+        }
+        mma_commit_pair(&sm.empty[s]);     // both CTAs may refill the stage
+        mma_commit_pair(&sm.acc_full[b]);  // both CTAs' sums of the block are ready
+      }
+    }
+    __syncwarp();
+  } else {
+    const int quarter = warp & 3, col0 = (warp >> 2) * kAccCols;
+    float2 acc[kAccCols / 2];
+#pragma unroll
+    for (int j = 0; j < kAccCols / 2; ++j) acc[j] = make_float2(0.f, 0.f);
+    bool ok = true;
+    const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)col0;
+    const uint32_t leader_empty0 = map_to_rank(&sm.acc_empty[0], 0);
+    const uint32_t leader_empty1 = map_to_rank(&sm.acc_empty[1], 0);
+    for (int kb = 0; kb < nk; ++kb) {
+      const int b = kb & 1;
+      ok = mamba_scan::mbar_wait(&sm.acc_full[b], (uint32_t)(kb >> 1) & 1u, &g_gemm_device_error);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+      const uint32_t t = lane_base + (uint32_t)(b * BN);
+      constexpr int kMax = 32;
+#pragma unroll
+      for (int c0 = 0; c0 < kAccCols; c0 += kMax) {
+        uint32_t v[kMax];
+        tmem_ld32(t + (uint32_t)c0, v);
+        tmem_wait();
+#pragma unroll
+        for (int j = 0; j < kMax / 2; ++j)
+          acc[c0 / 2 + j] = __fadd2_rn(acc[c0 / 2 + j], make_float2(__uint_as_float(v[2 * j]),
+                                                                    __uint_as_float(v[2 * j + 1])));
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(b ? leader_empty1 : leader_empty0);
+    }
+    // the last block's commit reached this CTA after every MMA of the pair
+    // completed: both CTAs' stages have landed and been read
+    if (__all_sync(0xffffffffu, ok))
+      store_sums<kAccCols>(p, acc, (int64_t)m0 + quarter * 32, (int64_t)n0 + col0,
+                           reinterpret_cast<float*>(&sm) + warp * kStoreScratch<kAccCols>, lane);
+  }
+  tc_fence_before();
+  cluster_sync_all();  // the pair is done with TMEM and with each other's barriers
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                  "r"(C::kTmemCols)
                  : "memory");
   }
@@ -500,6 +820,45 @@ cudaError_t launch_gemm(const mamba_gemm::GemmMaps& maps, const mamba_gemm::Gemm
                                 C::kSmemBytes, st, maps, p);
 }
 
+// CTA pairs (gemm_tf32x3_pair_kernel): the pair tile width with the fewest
+// waves x (128 + BN/2) (per CTA and K block it streams (2 * 128 + 2 * BN/2)
+// rows of 128 bytes), or 0 when single CTAs cost less ((128 + BN) per CTA);
+// ties go to pairs.
+int pair_width(int64_t M, int64_t N, int sms, int single_bn) {
+  const int64_t m_tiles = (M + mamba_gemm::BM - 1) / mamba_gemm::BM;
+  const int64_t single = (m_tiles * ((N + single_bn - 1) / single_bn) + sms - 1) / sms *
+                         (mamba_gemm::BM + single_bn);
+  const int64_t pairs_m = (M + 255) / 256;
+  int best = 0;
+  int64_t best_cost = single;
+  for (int bn : {256, 192, 128, 64}) {
+    const int64_t ctas = 2 * pairs_m * ((N + bn - 1) / bn);
+    const int64_t cost = (ctas + sms - 1) / sms * (mamba_gemm::BM + bn / 2);
+    if (cost <= best_cost) {
+      best = bn;
+      best_cost = cost;
+    }
+  }
+  return best;
+}
+
+template <class C>
+cudaError_t launch_gemm_pair(const mamba_gemm::GemmMaps& maps, const mamba_gemm::GemmParams& p,
+                             cudaStream_t st) {
+  static std::once_flag attr_once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(attr_once, [] {
+    attr_err = cudaFuncSetAttribute(mamba_gemm::gemm_tf32x3_pair_kernel<C>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)C::kSmemBytes);
+  });
+  if (attr_err != cudaSuccess) return attr_err;
+  const int64_t pairs_m = (p.M + 255) / 256, n_tiles = (p.N + C::BN - 1) / C::BN;
+  return mamba_scan::launch_pdl(mamba_gemm::gemm_tf32x3_pair_kernel<C>,
+                                dim3((unsigned)(2 * pairs_m), (unsigned)n_tiles),
+                                dim3(C::kThreads), C::kSmemBytes, st, maps, p);
+}
+
 bool overlap(const void* a, int64_t abytes, const void* b, int64_t bbytes) {
   const auto a0 = reinterpret_cast<uintptr_t>(a), b0 = reinterpret_cast<uintptr_t>(b);
   return a0 < b0 + (uintptr_t)bbytes && b0 < a0 + (uintptr_t)abytes;
@@ -585,19 +944,26 @@ int mamba_gemm_tf32x3(const float* a_hi, const float* a_lo, int64_t lda, const f
   if (m_tiles > 0x7FFFFFFF || (N + 63) / 64 > 65535)
     return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "gemm_tf32x3: too many tiles");
   const int bn = tile_width(M, N, device_sms());
+  const int pair_bn = pair_width(M, N, device_sms(), bn);
   auto enc = gemm_encode_fn();
   mamba_gemm::GemmMaps maps;
   std::memset(&maps, 0, sizeof maps);
+  const int b_box = pair_bn ? pair_bn / 2 : bn;  // a CTA of a pair holds half of B's tile
   if (!enc || !encode_operand(enc, &maps.a_hi, a_hi, M, K, lda, mamba_gemm::BM) ||
       !encode_operand(enc, &maps.a_lo, a_lo, M, K, lda, mamba_gemm::BM) ||
-      !encode_operand(enc, &maps.b_hi, b_hi, N, K, ldb, bn) ||
-      !encode_operand(enc, &maps.b_lo, b_lo, N, K, ldb, bn))
+      !encode_operand(enc, &maps.b_hi, b_hi, N, K, ldb, b_box) ||
+      !encode_operand(enc, &maps.b_lo, b_lo, N, K, ldb, b_box))
     return set_last_error(MAMBA_SCAN_ERR_CUDA, "gemm_tf32x3: tensor map encoding failed");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   mamba_gemm::GemmParams p{c, c_in, ldc_m, ldc_n, (int)M, (int)N, (int)K};
-  const cudaError_t e = bn == 192   ? launch_gemm<mamba_gemm::Cfg192>(maps, p, m_tiles, st)
-                        : bn == 128 ? launch_gemm<mamba_gemm::Cfg128>(maps, p, m_tiles, st)
-                                    : launch_gemm<mamba_gemm::Cfg64>(maps, p, m_tiles, st);
+  cudaError_t e;
+  if (pair_bn == 256) e = launch_gemm_pair<mamba_gemm::Cfg2x256>(maps, p, st);
+  else if (pair_bn == 192) e = launch_gemm_pair<mamba_gemm::Cfg2x192>(maps, p, st);
+  else if (pair_bn == 128) e = launch_gemm_pair<mamba_gemm::Cfg2x128>(maps, p, st);
+  else if (pair_bn == 64) e = launch_gemm_pair<mamba_gemm::Cfg2x64>(maps, p, st);
+  else if (bn == 192) e = launch_gemm<mamba_gemm::Cfg192>(maps, p, m_tiles, st);
+  else if (bn == 128) e = launch_gemm<mamba_gemm::Cfg128>(maps, p, m_tiles, st);
+  else e = launch_gemm<mamba_gemm::Cfg64>(maps, p, m_tiles, st);
   if (e != cudaSuccess) return set_last_error(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
   return MAMBA_SCAN_OK;
 }

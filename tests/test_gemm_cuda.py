@@ -50,6 +50,12 @@ CASES = [
     # 192-column tiles (chosen when they take fewer waves): ragged M, N, K
     (3000, 1000, 100, False, False),
     (2900, 900, 40, True, True),
+    # CTA pairs with 256-column tiles (the LM head's choice): a pair whose
+    # second CTA lies wholly past M, ragged N and K
+    (300, 7500, 100, False, True),
+    (1024, 3500, 768, True, False),
+    # few rows, many columns: single CTAs with 192-column tiles
+    (64, 19008, 40, False, False),
 ]
 
 
