@@ -245,6 +245,32 @@ MAMBA_SCAN_API int mamba_gemm_tf32x3(const float* a_hi, const float* a_lo, int64
                                      const float* c_in, float* c, int64_t ldc_m, int64_t ldc_n,
                                      int64_t M, int64_t N, int64_t K, void* stream);
 
+/*
+ * Workspace bytes that let mamba_gemm_tf32x3_ws split the K dimension of an
+ * M x N x K product across CTAs: nonzero when the output has too few tiles
+ * to keep the GPU's SMs busy (e.g. a 768 x 1024 output with K = 1536), 0
+ * when the product runs unsplit. Depends on the current device's SM count.
+ */
+MAMBA_SCAN_API size_t mamba_gemm_tf32x3_workspace_size(int64_t M, int64_t N, int64_t K);
+
+/*
+ * mamba_gemm_tf32x3 with a caller-provided device workspace (16-byte
+ * aligned, not overlapping the operands, C or C_in; its contents need no
+ * initialisation). When mamba_gemm_tf32x3_workspace_size(M, N, K) is
+ * nonzero, the product is computed as that many bytes of partial products
+ * (K split into ranges), which a second kernel adds in a fixed order, then
+ * C_in: the result does not depend on scheduling, and differs from the
+ * unsplit product only by the order of the fp32 additions. workspace_bytes
+ * below that size -> MAMBA_SCAN_ERR_WORKSPACE; workspace NULL runs unsplit
+ * (mamba_gemm_tf32x3). Calls sharing a workspace must be ordered (one
+ * stream, or synchronised).
+ */
+MAMBA_SCAN_API int mamba_gemm_tf32x3_ws(const float* a_hi, const float* a_lo, int64_t lda,
+                                        const float* b_hi, const float* b_lo, int64_t ldb,
+                                        const float* c_in, float* c, int64_t ldc_m,
+                                        int64_t ldc_n, int64_t M, int64_t N, int64_t K,
+                                        void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

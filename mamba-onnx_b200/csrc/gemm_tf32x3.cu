@@ -108,6 +108,11 @@ struct GemmParams {
   const float* c_in;  // NULL: C = A B^T; else C = C_in + A B^T (C's strides)
   int64_t ldc_m, ldc_n;
   int M, N, K;
+  // split K: grid.z = the number of splits; split z takes K blocks
+  // [z * kb_per_split, (z + 1) * kb_per_split) and writes its partial sums
+  // at c + z * slice (slice 0 and kb_per_split = all blocks when unsplit)
+  int kb_per_split;
+  int64_t slice;
 };
 
 __device__ int g_gemm_device_error = 0;
@@ -199,7 +204,8 @@ __device__ __forceinline__ void tmem_wait() {
 template <int kCols>
 constexpr int kStoreScratch = 32 * (kCols + 1);
 
-// Writes one accumulator warp's block of sums to C: lane l holds the kCols
+// Writes one accumulator warp's block of sums to C (at `c`, p's strides and
+// sizes; a split's partial slice or C itself): lane l holds the kCols
 // sums of row m_base + l, columns n_base... (acc[j/2].x / .y = column j),
 // C[m][n] = (C_in[m][n] +) sum. C_in may be C itself: every element is read
 // and written by the same thread, and each batch of reads is issued before
@@ -209,9 +215,9 @@ constexpr int kStoreScratch = 32 * (kCols + 1);
 // `scratch` (this warp's kStoreScratch<kCols> floats) and comes back one row
 // at a time, the lanes on consecutive columns.
 template <int kCols>
-__device__ __forceinline__ void store_sums(const GemmParams& p, const float2 (&acc)[kCols / 2],
-                                           int64_t m_base, int64_t n_base, float* scratch,
-                                           int lane) {
+__device__ __forceinline__ void store_sums(const GemmParams& p, float* c,
+                                           const float2 (&acc)[kCols / 2], int64_t m_base,
+                                           int64_t n_base, float* scratch, int lane) {
   constexpr int kBatch = 16;
   if (p.ldc_m == 1) {
     const int64_t m = m_base + lane;
@@ -228,7 +234,7 @@ __device__ __forceinline__ void store_sums(const GemmParams& p, const float2 (&a
       for (int j = 0; j < kBatch; ++j) {
         const int64_t n = n_base + j0 + j;
         const float a = ((j0 + j) & 1) ? acc[(j0 + j) / 2].y : acc[(j0 + j) / 2].x;
-        if (m_ok && n < p.N) p.c[m + n * p.ldc_n] = p.c_in ? in[j] + a : a;
+        if (m_ok && n < p.N) c[m + n * p.ldc_n] = p.c_in ? in[j] + a : a;
       }
     }
     return;
@@ -257,7 +263,7 @@ __device__ __forceinline__ void store_sums(const GemmParams& p, const float2 (&a
 #pragma unroll
       for (int h = 0; h < kPerRow; ++h) {
         const int64_t n = n_base + h * 32 + lane;
-        if (m < p.M && n < p.N) p.c[m * p.ldc_m + n * p.ldc_n] = p.c_in ? in[r][h] + v[r][h] : v[r][h];
+        if (m < p.M && n < p.N) c[m * p.ldc_m + n * p.ldc_n] = p.c_in ? in[r][h] + v[r][h] : v[r][h];
       }
     }
   }
@@ -279,7 +285,9 @@ __global__ void __launch_bounds__(C::kThreads, 1)
   // M tiles vary fastest: the CTAs running together share B tiles (the
   // larger operand of a wide GEMM such as an LM head), read from HBM once
   const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
-  const int nk = (p.K + BK - 1) / BK;
+  // this CTA's K blocks: [kb_begin, kb_begin + nk)
+  const int kb_begin = (int)blockIdx.z * p.kb_per_split;
+  const int nk = min((p.K + BK - 1) / BK - kb_begin, p.kb_per_split);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -323,7 +331,7 @@ __global__ void __launch_bounds__(C::kThreads, 1)
                                    &g_gemm_device_error))
           break;
         mamba_scan::mbar_arrive_expect_tx(&sm.full[s], C::kStageBytes);
-        const int k0 = kb * BK;
+        const int k0 = (kb_begin + kb) * BK;
         tma_load_2d(sm.a_hi[s], &maps.a_hi, &sm.full[s], k0, m0);
         tma_load_2d(sm.a_lo[s], &maps.a_lo, &sm.full[s], k0, m0);
         tma_load_2d(sm.b_hi[s], &maps.b_hi, &sm.full[s], k0, n0);
@@ -401,7 +409,8 @@ __global__ void __launch_bounds__(C::kThreads, 1)
     // after the last block every stage has landed and been read by the
     // MMAs: the stage buffers are free for the transposes of the stores
     if (__all_sync(0xffffffffu, ok))
-      store_sums<kAccCols>(p, acc, (int64_t)m0 + quarter * 32, (int64_t)n0 + col0,
+      store_sums<kAccCols>(p, p.c + (int64_t)blockIdx.z * p.slice, acc,
+                           (int64_t)m0 + quarter * 32, (int64_t)n0 + col0,
                            reinterpret_cast<float*>(&sm) + warp * kStoreScratch<kAccCols>, lane);
   }
   tc_fence_before();
@@ -536,7 +545,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(C::kThreads, 1)
   // pairs along M vary fastest; this CTA's A rows and B rows
   const int m0 = (blockIdx.x >> 1) * 256 + (int)rank * BM;
   const int n0 = blockIdx.y * BN;
-  const int nk = (p.K + BK - 1) / BK;
+  // this CTA's K blocks: [kb_begin, kb_begin + nk)
+  const int kb_begin = (int)blockIdx.z * p.kb_per_split;
+  const int nk = min((p.K + BK - 1) / BK - kb_begin, p.kb_per_split);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -580,7 +591,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(C::kThreads, 1)
         // the leader's barrier counts both CTAs' bytes of the stage
         if (rank == 0) mamba_scan::mbar_arrive_expect_tx(&sm.full[s], 2 * C::kStageBytes);
         const uint32_t bar = map_to_rank(&sm.full[s], 0);
-        const int k0 = kb * BK;
+        const int k0 = (kb_begin + kb) * BK;
         tma_load_2d_pair(sm.a_hi[s], &maps.a_hi, bar, k0, m0);
         tma_load_2d_pair(sm.a_lo[s], &maps.a_lo, bar, k0, m0);
         tma_load_2d_pair(sm.b_hi[s], &maps.b_hi, bar, k0, n0 + (int)rank * C::kHalfN);
@@ -651,7 +662,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(C::kThreads, 1)
     // the last block's commit reached this CTA after every MMA of the pair
     // completed: both CTAs' stages have landed and been read
     if (__all_sync(0xffffffffu, ok))
-      store_sums<kAccCols>(p, acc, (int64_t)m0 + quarter * 32, (int64_t)n0 + col0,
+      store_sums<kAccCols>(p, p.c + (int64_t)blockIdx.z * p.slice, acc,
+                           (int64_t)m0 + quarter * 32, (int64_t)n0 + col0,
                            reinterpret_cast<float*>(&sm) + warp * kStoreScratch<kAccCols>, lane);
   }
   tc_fence_before();
@@ -661,6 +673,50 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(C::kThreads, 1)
     asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                  "r"(C::kTmemCols)
                  : "memory");
+  }
+}
+
+// ------------------------------------------------------- split-K reduction
+
+// C = (C_in +) the sum of the `splits` partial products in ws, added in split
+// order (ws[0] + ws[1] + ...; fixed, so results do not depend on which CTA
+// finished first). The partials are compact M x N slices `slice` floats
+// apart, laid out like C: element (m, n) at m + n * M when C is column-major
+// (col_major), m * N + n otherwise. `dense`: C and C_in (when given) are that
+// same compact layout, 16-byte aligned, and M * N is a multiple of 4, so
+// whole float4s go at once.
+__global__ void __launch_bounds__(256)
+    split_reduce_kernel(const float* __restrict__ ws, int splits, int64_t slice, int M, int N,
+                        int col_major, int dense, float* c, const float* c_in, int64_t ldc_m,
+                        int64_t ldc_n) {
+  mamba_scan::pdl_wait();  // the partial products are complete and visible
+  mamba_scan::pdl_trigger();
+  const int64_t total = (int64_t)M * N;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  if (dense) {
+    for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < total / 4; v += stride) {
+      float4 s = reinterpret_cast<const float4*>(ws)[v];
+      for (int z = 1; z < splits; ++z) {
+        const float4 t = reinterpret_cast<const float4*>(ws + z * slice)[v];
+        s.x += t.x;
+        s.y += t.y;
+        s.z += t.z;
+        s.w += t.w;
+      }
+      if (c_in) {
+        const float4 t = reinterpret_cast<const float4*>(c_in)[v];
+        s = make_float4(t.x + s.x, t.y + s.y, t.z + s.z, t.w + s.w);
+      }
+      reinterpret_cast<float4*>(c)[v] = s;
+    }
+    return;
+  }
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    float s = ws[i];
+    for (int z = 1; z < splits; ++z) s += ws[z * slice + i];
+    const int64_t m = col_major ? i % M : i / N, n = col_major ? i / M : i % N;
+    const int64_t o = m * ldc_m + n * ldc_n;
+    c[o] = c_in ? c_in[o] + s : s;
   }
 }
 
@@ -805,7 +861,7 @@ int tile_width(int64_t M, int64_t N, int sms) {
 
 template <class C>
 cudaError_t launch_gemm(const mamba_gemm::GemmMaps& maps, const mamba_gemm::GemmParams& p,
-                        int64_t m_tiles, cudaStream_t st) {
+                        int64_t m_tiles, int splits, cudaStream_t st) {
   static std::once_flag attr_once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(attr_once, [] {
@@ -816,8 +872,8 @@ cudaError_t launch_gemm(const mamba_gemm::GemmMaps& maps, const mamba_gemm::Gemm
   if (attr_err != cudaSuccess) return attr_err;
   const int64_t n_tiles = (p.N + C::BN - 1) / C::BN;
   return mamba_scan::launch_pdl(mamba_gemm::gemm_tf32x3_kernel<C>,
-                                dim3((unsigned)m_tiles, (unsigned)n_tiles), dim3(C::kThreads),
-                                C::kSmemBytes, st, maps, p);
+                                dim3((unsigned)m_tiles, (unsigned)n_tiles, (unsigned)splits),
+                                dim3(C::kThreads), C::kSmemBytes, st, maps, p);
 }
 
 // CTA pairs (gemm_tf32x3_pair_kernel): the pair tile width with the fewest
@@ -842,9 +898,74 @@ int pair_width(int64_t M, int64_t N, int sms, int single_bn) {
   return best;
 }
 
+// Tiling of one product: CTA pairs of width pair_bn (0: single CTAs of
+// width bn), K split `splits` ways (1: unsplit) with kb_per_split K blocks
+// each and partial slices `slice` floats apart.
+struct GemmPlan {
+  int pair_bn, bn, splits, kb_per_split;
+  int64_t slice;
+  size_t workspace_bytes() const { return splits > 1 ? (size_t)splits * slice * 4 : 0; }
+};
+
+// Modelled SM cycles of a tiling, for choosing whether to split K: a K block
+// costs a CTA the larger of its MMAs (12 x 128 x BN x 8 tf32 FMAs at ~1925
+// per cycle) and its operand delivery ((2 * 128 + 2 * B rows) x 128 bytes at
+// ~50 bytes per cycle per SM with every SM streaming); a tile adds ~10k
+// cycles (start-up, pipeline fill and drain, stores); a split adds the
+// reduction (one launch, then the partials and C through L2 at ~8 KB per
+// cycle).
+double plan_cycles(int64_t M, int64_t N, int64_t K, int sms, int pair_bn, int bn, int splits) {
+  const int64_t nk = (K + mamba_gemm::BK - 1) / mamba_gemm::BK;
+  const int64_t kbs = (nk + splits - 1) / splits;
+  const int w = pair_bn ? pair_bn : bn;
+  const int b_rows = pair_bn ? pair_bn / 2 : bn;
+  const double block = std::max(6.4 * w, (2.0 * mamba_gemm::BM + 2.0 * b_rows) * 128.0 / 50.0);
+  const int64_t ctas = (pair_bn ? 2 * ((M + 255) / 256) : (M + mamba_gemm::BM - 1) / mamba_gemm::BM) *
+                       ((N + w - 1) / w) * splits;
+  const int64_t waves = (ctas + sms - 1) / sms;
+  double t = (double)waves * ((double)kbs * block + 10000.0);
+  if (splits > 1) t += 2000.0 + (double)M * N * (splits + 2) * 4.0 / 8192.0;
+  return t;
+}
+
+// The tiling of an M x N x K product: the unsplit choice of tile_width and
+// pair_width, or, when the output has too few tiles to keep the SMs busy,
+// the split of K (2..16 ways, every split at least one K block) that the
+// model makes at least 25% faster.
+GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int sms, bool allow_split) {
+  GemmPlan plan;
+  plan.bn = tile_width(M, N, sms);
+  plan.pair_bn = pair_width(M, N, sms, plan.bn);
+  plan.splits = 1;
+  plan.kb_per_split = (int)((K + mamba_gemm::BK - 1) / mamba_gemm::BK);
+  plan.slice = 0;
+  if (!allow_split) return plan;
+  const int64_t nk = plan.kb_per_split;
+  const double unsplit = plan_cycles(M, N, K, sms, plan.pair_bn, plan.bn, 1);
+  double best = 0.75 * unsplit;
+  for (int pair_bn : {256, 192, 128, 64, 0})
+    for (int bn : {192, 128, 64}) {
+      if (pair_bn && bn != 192) continue;  // bn is unused with pairs
+      for (int splits = 2; splits <= 16; ++splits) {
+        const int64_t kbs = (nk + splits - 1) / splits;
+        if (kbs * (splits - 1) >= nk) break;  // the last split would be empty
+        const double t = plan_cycles(M, N, K, sms, pair_bn, bn, splits);
+        if (t < best) {
+          best = t;
+          plan.pair_bn = pair_bn;
+          plan.bn = bn;
+          plan.splits = splits;
+          plan.kb_per_split = (int)kbs;
+        }
+      }
+    }
+  if (plan.splits > 1) plan.slice = (M * N + 3) / 4 * 4;  // 16-byte aligned slices
+  return plan;
+}
+
 template <class C>
 cudaError_t launch_gemm_pair(const mamba_gemm::GemmMaps& maps, const mamba_gemm::GemmParams& p,
-                             cudaStream_t st) {
+                             int splits, cudaStream_t st) {
   static std::once_flag attr_once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(attr_once, [] {
@@ -855,7 +976,7 @@ cudaError_t launch_gemm_pair(const mamba_gemm::GemmMaps& maps, const mamba_gemm:
   if (attr_err != cudaSuccess) return attr_err;
   const int64_t pairs_m = (p.M + 255) / 256, n_tiles = (p.N + C::BN - 1) / C::BN;
   return mamba_scan::launch_pdl(mamba_gemm::gemm_tf32x3_pair_kernel<C>,
-                                dim3((unsigned)(2 * pairs_m), (unsigned)n_tiles),
+                                dim3((unsigned)(2 * pairs_m), (unsigned)n_tiles, (unsigned)splits),
                                 dim3(C::kThreads), C::kSmemBytes, st, maps, p);
 }
 
@@ -906,10 +1027,25 @@ int mamba_split_tf32(const float* x, int64_t rows, int64_t cols, int64_t ldx, in
   return MAMBA_SCAN_OK;
 }
 
+size_t mamba_gemm_tf32x3_workspace_size(int64_t M, int64_t N, int64_t K) {
+  if (M <= 0 || N <= 0 || K <= 0 || M > ((int64_t)1 << 30) || N > ((int64_t)1 << 30) ||
+      K > ((int64_t)1 << 30))
+    return 0;
+  return plan_gemm(M, N, K, device_sms(), true).workspace_bytes();
+}
+
 int mamba_gemm_tf32x3(const float* a_hi, const float* a_lo, int64_t lda, const float* b_hi,
                       const float* b_lo, int64_t ldb, const float* c_in, float* c,
                       int64_t ldc_m, int64_t ldc_n, int64_t M, int64_t N, int64_t K,
                       void* stream) {
+  return mamba_gemm_tf32x3_ws(a_hi, a_lo, lda, b_hi, b_lo, ldb, c_in, c, ldc_m, ldc_n, M, N, K,
+                              nullptr, 0, stream);
+}
+
+int mamba_gemm_tf32x3_ws(const float* a_hi, const float* a_lo, int64_t lda, const float* b_hi,
+                         const float* b_lo, int64_t ldb, const float* c_in, float* c,
+                         int64_t ldc_m, int64_t ldc_n, int64_t M, int64_t N, int64_t K,
+                         void* workspace, size_t workspace_bytes, void* stream) {
   using mamba_scan::set_last_error;
   if (M < 0 || N < 0 || K < 0)
     return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "gemm_tf32x3: negative size");
@@ -943,28 +1079,70 @@ int mamba_gemm_tf32x3(const float* a_hi, const float* a_lo, int64_t lda, const f
   const int64_t m_tiles = (M + mamba_gemm::BM - 1) / mamba_gemm::BM;
   if (m_tiles > 0x7FFFFFFF || (N + 63) / 64 > 65535)
     return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "gemm_tf32x3: too many tiles");
-  const int bn = tile_width(M, N, device_sms());
-  const int pair_bn = pair_width(M, N, device_sms(), bn);
+  const GemmPlan plan = plan_gemm(M, N, K, device_sms(), workspace != nullptr);
+  const bool split = plan.splits > 1;
+  if (split) {
+    if (workspace_bytes < plan.workspace_bytes())
+      return set_last_error(MAMBA_SCAN_ERR_WORKSPACE,
+                            "gemm_tf32x3: the workspace holds " + std::to_string(workspace_bytes) +
+                                " bytes, this product needs " +
+                                std::to_string(plan.workspace_bytes()) +
+                                " (mamba_gemm_tf32x3_workspace_size)");
+    if (!al16(workspace))
+      return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT,
+                            "gemm_tf32x3: the workspace must be 16-byte aligned");
+    const int64_t ws_bytes = (int64_t)plan.workspace_bytes();
+    for (int i = 0; i < 4; ++i)
+      if (overlap(workspace, ws_bytes, ops[i], op_bytes[i]))
+        return set_last_error(MAMBA_SCAN_ERR_ALIASING,
+                              "gemm_tf32x3: the workspace overlaps an operand");
+    if (overlap(workspace, ws_bytes, c, c_bytes) ||
+        (c_in && overlap(workspace, ws_bytes, c_in, c_bytes)))
+      return set_last_error(MAMBA_SCAN_ERR_ALIASING, "gemm_tf32x3: the workspace overlaps C");
+  }
   auto enc = gemm_encode_fn();
   mamba_gemm::GemmMaps maps;
   std::memset(&maps, 0, sizeof maps);
-  const int b_box = pair_bn ? pair_bn / 2 : bn;  // a CTA of a pair holds half of B's tile
+  const int b_box = plan.pair_bn ? plan.pair_bn / 2 : plan.bn;  // a CTA of a pair holds half of B's tile
   if (!enc || !encode_operand(enc, &maps.a_hi, a_hi, M, K, lda, mamba_gemm::BM) ||
       !encode_operand(enc, &maps.a_lo, a_lo, M, K, lda, mamba_gemm::BM) ||
       !encode_operand(enc, &maps.b_hi, b_hi, N, K, ldb, b_box) ||
       !encode_operand(enc, &maps.b_lo, b_lo, N, K, ldb, b_box))
     return set_last_error(MAMBA_SCAN_ERR_CUDA, "gemm_tf32x3: tensor map encoding failed");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  mamba_gemm::GemmParams p{c, c_in, ldc_m, ldc_n, (int)M, (int)N, (int)K};
+  // a split writes compact partial slices laid out like C (column-major when
+  // m is C's faster index), without C_in; the reduction then writes C
+  const bool col_major = ldc_m < ldc_n;
+  mamba_gemm::GemmParams p{c, c_in, ldc_m, ldc_n, (int)M, (int)N, (int)K,
+                           plan.kb_per_split, 0};
+  if (split) {
+    p.c = static_cast<float*>(workspace);
+    p.c_in = nullptr;
+    p.ldc_m = col_major ? 1 : N;
+    p.ldc_n = col_major ? M : 1;
+    p.slice = plan.slice;
+  }
+  const int sp = plan.splits;
   cudaError_t e;
-  if (pair_bn == 256) e = launch_gemm_pair<mamba_gemm::Cfg2x256>(maps, p, st);
-  else if (pair_bn == 192) e = launch_gemm_pair<mamba_gemm::Cfg2x192>(maps, p, st);
-  else if (pair_bn == 128) e = launch_gemm_pair<mamba_gemm::Cfg2x128>(maps, p, st);
-  else if (pair_bn == 64) e = launch_gemm_pair<mamba_gemm::Cfg2x64>(maps, p, st);
-  else if (bn == 192) e = launch_gemm<mamba_gemm::Cfg192>(maps, p, m_tiles, st);
-  else if (bn == 128) e = launch_gemm<mamba_gemm::Cfg128>(maps, p, m_tiles, st);
-  else e = launch_gemm<mamba_gemm::Cfg64>(maps, p, m_tiles, st);
+  if (plan.pair_bn == 256) e = launch_gemm_pair<mamba_gemm::Cfg2x256>(maps, p, sp, st);
+  else if (plan.pair_bn == 192) e = launch_gemm_pair<mamba_gemm::Cfg2x192>(maps, p, sp, st);
+  else if (plan.pair_bn == 128) e = launch_gemm_pair<mamba_gemm::Cfg2x128>(maps, p, sp, st);
+  else if (plan.pair_bn == 64) e = launch_gemm_pair<mamba_gemm::Cfg2x64>(maps, p, sp, st);
+  else if (plan.bn == 192) e = launch_gemm<mamba_gemm::Cfg192>(maps, p, m_tiles, sp, st);
+  else if (plan.bn == 128) e = launch_gemm<mamba_gemm::Cfg128>(maps, p, m_tiles, sp, st);
+  else e = launch_gemm<mamba_gemm::Cfg64>(maps, p, m_tiles, sp, st);
   if (e != cudaSuccess) return set_last_error(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
+  if (split) {
+    const bool dense = (col_major ? (ldc_m == 1 && ldc_n == M) : (ldc_n == 1 && ldc_m == N)) &&
+                       al16(c) && (!c_in || al16(c_in)) && (M * N) % 4 == 0;
+    const int64_t items = dense ? M * N / 4 : M * N;
+    const int64_t blocks = std::min<int64_t>((items + 255) / 256, (int64_t)device_sms() * 8);
+    e = mamba_scan::launch_pdl(mamba_gemm::split_reduce_kernel, dim3((unsigned)blocks), dim3(256),
+                               0, st, static_cast<const float*>(workspace), plan.splits,
+                               plan.slice, (int)M, (int)N, (int)col_major, (int)dense, c, c_in,
+                               ldc_m, ldc_n);
+    if (e != cudaSuccess) return set_last_error(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
+  }
   return MAMBA_SCAN_OK;
 }
 

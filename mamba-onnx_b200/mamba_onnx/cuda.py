@@ -119,6 +119,12 @@ def library() -> ctypes.CDLL:
         lib.mamba_gemm_tf32x3.restype = ctypes.c_int
         lib.mamba_gemm_tf32x3.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64] * 2 + \
             [ctypes.c_void_p] * 2 + [ctypes.c_int64] * 5 + [ctypes.c_void_p]
+        lib.mamba_gemm_tf32x3_ws.restype = ctypes.c_int
+        lib.mamba_gemm_tf32x3_ws.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64] * 2 + \
+            [ctypes.c_void_p] * 2 + [ctypes.c_int64] * 5 + \
+            [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
+        lib.mamba_gemm_tf32x3_workspace_size.restype = ctypes.c_size_t
+        lib.mamba_gemm_tf32x3_workspace_size.argtypes = [ctypes.c_int64] * 3
         _lib = lib
     return _lib
 
@@ -582,13 +588,21 @@ def split_tf32(x, transpose: bool = False, out: SplitTF32 | None = None,
     return out
 
 
+def gemm_workspace_size(M: int, N: int, K: int) -> int:
+    """Workspace bytes with which gemm_tf32x3 splits K for an M x N x K
+    product (0: it runs unsplit; mamba_gemm_tf32x3_workspace_size)."""
+    return int(library().mamba_gemm_tf32x3_workspace_size(M, N, K))
+
+
 def gemm_tf32x3(a: SplitTF32, b: SplitTF32, c, *, transpose_c: bool = False,
-                c_in=None, stream=None):
+                c_in=None, stream=None, workspace=None):
     """c = (c_in +) a @ b.T on the tensor cores, fp32-accurate (3xTF32): a
     [M][K], b [N][K] split operands; c a CUDA float32 tensor viewed as [M, N]
     (or, with ``transpose_c``, as [N, M]: c[n][m] receives element (m, n));
     c_in None or a tensor with c's shape and strides (c itself allowed).
-    Returns c."""
+    ``workspace``: None, or a CUDA tensor of at least
+    gemm_workspace_size(M, N, K) bytes (mamba_gemm_tf32x3_ws), with which a
+    product of few output tiles splits K across the SMs. Returns c."""
     import torch
 
     if a.cols != b.cols:
@@ -604,8 +618,12 @@ def gemm_tf32x3(a: SplitTF32, b: SplitTF32, c, *, transpose_c: bool = False,
                              or not c_in.is_cuda or c_in.dtype != torch.float32):
         raise ValueError("c_in must be a CUDA float32 tensor with c's shape and strides")
     st = stream if stream is not None else torch.cuda.current_stream(c.device)
-    rc = library().mamba_gemm_tf32x3(_ptr(a.hi), _ptr(a.lo), a.ld, _ptr(b.hi), _ptr(b.lo), b.ld,
-                                     _ptr(c_in), _ptr(c), ldc_m, ldc_n, M, N, K, st.cuda_stream)
+    if workspace is not None and (not workspace.is_cuda or not workspace.is_contiguous()):
+        raise ValueError("workspace must be a contiguous CUDA tensor")
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    rc = library().mamba_gemm_tf32x3_ws(_ptr(a.hi), _ptr(a.lo), a.ld, _ptr(b.hi), _ptr(b.lo),
+                                        b.ld, _ptr(c_in), _ptr(c), ldc_m, ldc_n, M, N, K,
+                                        _ptr(workspace), ws_bytes, st.cuda_stream)
     if rc != STATUS_OK:
         _raise(rc, "gemm_tf32x3")
     return c

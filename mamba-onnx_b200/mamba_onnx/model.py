@@ -110,15 +110,35 @@ class _SplitWeight:
         return self.split
 
 
+_gemm_workspaces = {}
+
+
+def _gemm_workspace(device, nbytes: int):
+    """The tensor-core GEMM's split-K workspace (cuda.gemm_workspace_size) for
+    the current stream of ``device``: one buffer per device and stream, so
+    that the calls sharing it are ordered; grown on demand. None for 0 bytes."""
+    if nbytes == 0:
+        return None
+    key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+    ws = _gemm_workspaces.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        _gemm_workspaces[key] = ws
+    return ws
+
+
 def add_out_proj(h, y, weight, split=None):
     """h + y^T W^T for h [B, L, d], y [B, D, L]; the sum is the GEMM's own
-    accumulation (addmm, or the tensor-core GEMM's c_in), not a separate kernel."""
+    accumulation (addmm, or the tensor-core GEMM's c_in), not a separate kernel.
+    A short sequence (few output tiles for a K of d_inner) splits K across the
+    SMs through a workspace."""
     if split is not None and _use_tc(h, h.shape[1]):
         w = split.get(weight)
         out = torch.empty_like(h)
+        ws = _gemm_workspace(h.device, cuda.gemm_workspace_size(w.rows, h.shape[1], w.cols))
         for b in range(h.shape[0]):  # out[b] [L, d] = h[b] + (y[b]^T [L, D]) W^T
             cuda.gemm_tf32x3(w, cuda.split_tf32(y[b], transpose=True), out[b],
-                             transpose_c=True, c_in=h[b])
+                             transpose_c=True, c_in=h[b], workspace=ws)
         return out
     if h.shape[0] == 1:
         return torch.addmm(h[0], y[0].t(), weight.t()).unsqueeze(0)

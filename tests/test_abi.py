@@ -144,6 +144,30 @@ def test_gemm_and_split_validate_before_launch():
     assert gemm(ldc_m=0) == 1
 
 
+def test_gemm_split_workspace_validates_before_launch():
+    """mamba_gemm_tf32x3_ws: the split of K is planned on the host; a short,
+    misaligned or overlapping workspace is rejected before any launch."""
+    lib = cuda.library()
+    f = 0x1000000  # 16 MiB apart
+    # the out_proj product of a 1024-token Mamba-130m forward splits K; the
+    # in_proj and LM-head products (enough output tiles) do not
+    need = cuda.gemm_workspace_size(768, 1024, 1536)
+    assert need > 0 and need % (768 * 1024 * 4) == 0
+    assert cuda.gemm_workspace_size(3072, 1024, 768) == 0
+    assert cuda.gemm_workspace_size(1024, 50280, 768) == 0
+    assert cuda.gemm_workspace_size(0, 1024, 1536) == 0
+
+    def gemm_ws(ws, ws_bytes, c=40 * f, c_in=None):
+        return lib.mamba_gemm_tf32x3_ws(f, 2 * f, 1536, 3 * f, 4 * f, 1536, c_in, c, 1, 768,
+                                        768, 1024, 1536, ws, ws_bytes, None)
+
+    assert gemm_ws(60 * f, need - 1) == 3 and b"workspace" in lib.mamba_scan_last_error()
+    assert gemm_ws(60 * f + 8, need) == 1 and b"aligned" in lib.mamba_scan_last_error()
+    assert gemm_ws(40 * f, need) == 4 and b"overlaps C" in lib.mamba_scan_last_error()
+    assert gemm_ws(60 * f, need, c_in=60 * f + 4096) == 4
+    assert gemm_ws(2 * f, need) == 4 and b"operand" in lib.mamba_scan_last_error()
+
+
 def test_conv1d_step_validates_before_launch():
     lib = cuda.library()
     f = 0x100000

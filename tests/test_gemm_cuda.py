@@ -143,3 +143,52 @@ def test_gemm_is_deterministic(cuda_device):
     cuda.gemm_tf32x3(a, b, c2)
     assert torch.equal(c1, c2)
     assert cuda.check_device_error() == 0
+
+
+SPLIT_CASES = [
+    # M, N, K, transpose_c, accumulate: products with few output tiles,
+    # whose K the GEMM splits across the SMs through a workspace
+    (768, 1024, 1536, True, True),    # out_proj into the residual (C_in = C)
+    (768, 1024, 1536, False, False),  # row-major C (the float4 reduction)
+    (701, 999, 1500, False, True),    # ragged M, N, K, odd M * N: the scalar reduction
+    (80, 1024, 1536, True, False),
+    (64, 64, 4096, False, True),
+]
+
+
+@pytest.mark.parametrize("M,N,K,tc,acc", SPLIT_CASES)
+def test_gemm_split_k_matches_float64(cuda_device, M, N, K, tc, acc):
+    """Split K (partials in the workspace, fixed-order reduction): the same
+    accuracy bounds as the unsplit product, bit-identical on a second run,
+    and within fp32 rounding of the unsplit product."""
+    dev = cuda_device
+    need = cuda.gemm_workspace_size(M, N, K)
+    assert need > 0, "the case must split"
+    a = _rand((M, K), 21 + M, dev)
+    b = _rand((N, K), 22 + N, dev, scale=0.05)
+    c0 = _rand((N, M) if tc else (M, N), 23 + K, dev)
+    ws = torch.full((need,), 0xFF, dtype=torch.uint8, device=dev)  # NaN garbage
+    sa, sb = cuda.split_tf32(a), cuda.split_tf32(b)
+
+    def run(workspace):
+        c = c0.clone() if acc else torch.full_like(c0, float("nan"))
+        cuda.gemm_tf32x3(sa, sb, c, transpose_c=tc, c_in=c if acc else None,
+                         workspace=workspace)
+        return c
+
+    c = run(ws)
+    ref = a.double() @ b.double().t()
+    bound = a.double().abs() @ b.double().abs().t()
+    if tc:
+        ref, bound = ref.t(), bound.t()
+    if acc:
+        ref, bound = ref + c0.double(), bound + c0.double().abs()
+    err = (c.double() - ref).abs()
+    assert bool((err <= 1e-5 * bound + 1e-30).all()), float((err / (bound + 1e-30)).max())
+    assert torch.equal(run(ws), c)
+    unsplit = run(None)
+    assert float((c.double() - unsplit.double()).abs().max()) <= \
+        float((2e-6 * bound).max())
+    with pytest.raises(RuntimeError, match="workspace"):
+        run(ws[: need - 16])
+    assert cuda.check_device_error() == 0
