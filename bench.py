@@ -699,6 +699,7 @@ def run_model(args):
     torch.cuda.synchronize()
     scan_ms = timed(sgraph.replay, 20)
     launches_per_scan = 3 if cuda.workspace_size(SCAN_OP, B, D, L) > 0 else 1
+    out_proj_reduce = 1 if cuda.gemm_workspace_size(model.cfg.d_model, L, D) > 0 else 0
 
     # the same forward run eagerly, its 24 scans through the ONNX Runtime
     # custom-op entry (CreateKernelV2 once per op, KernelComputeV2 per call)
@@ -731,11 +732,12 @@ def run_model(args):
                     "h2d_bytes_per_step": host_ids.numel() * 8,
                     "d2h_bytes_per_step": host_last.numel() * 4, "ms_per_step": e2e_ms,
                     "path": "pinned token ids -> graph replay -> last-position logits to host"},
-            # this package's kernels per forward: per block RMSNorm, conv +
-            # SiLU, x_proj, two tf32 splits and two GEMMs (in_proj, out_proj)
-            # and the scan; then the final RMSNorm, its split and the LM-head
-            # GEMM
-            "gpu_launches": (model.cfg.n_layer * (7 + launches_per_scan) + 3) * args.steps,
+            # this package's kernels per forward: per block the RMSNorm that
+            # writes in_proj's tf32 operand, in_proj, conv + SiLU, x_proj, the
+            # scan, y's tf32 split, out_proj (and its split-K reduction);
+            # then the final RMSNorm (to the LM head's operand) and the LM head
+            "gpu_launches": (model.cfg.n_layer * (6 + launches_per_scan + out_proj_reduce) + 2)
+            * args.steps,
             "scan_ms_per_step": scan_ms,
             "ort_entry": {"ms_per_step": ort_ms, "value": world * B * L / (ort_ms * 1e-3),
                           "unit": MODEL_UNIT,

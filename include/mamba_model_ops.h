@@ -33,6 +33,17 @@ MAMBA_SCAN_API int mamba_rmsnorm(const float* x, const float* weight, float* y, 
                                  int64_t cols, float eps, void* stream);
 
 /*
+ * mamba_rmsnorm whose result goes straight into the operand form of
+ * mamba_gemm_tf32x3: hi and lo ([rows][ld], ld >= cols, both multiples of 4;
+ * x, weight, hi, lo 16-byte aligned and x, hi, lo not overlapping) receive
+ * exactly what mamba_split_tf32 would write for mamba_rmsnorm's y, without y
+ * being stored.
+ */
+MAMBA_SCAN_API int mamba_rmsnorm_split_tf32(const float* x, const float* weight, int64_t rows,
+                                            int64_t cols, float eps, float* hi, float* lo,
+                                            int64_t ld, void* stream);
+
+/*
  * Causal depthwise convolution over the sequence, then SiLU:
  *   y[b, d, t] = silu(bias[d] + sum_{k < width} weight[d, k] * x[b, d, t - (width-1) + k])
  * with x taken as 0 before t = 0 (torch's conv1d(groups=dim, padding=width-1)

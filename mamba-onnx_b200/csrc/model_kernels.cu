@@ -61,17 +61,47 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
+// tf32(v) rounded to nearest (ties away), as mamba_split_tf32 forms its hi
+// part; the lo part is tf32(v - hi).
+__device__ __forceinline__ float round_tf32(float v) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
+  return __uint_as_float(r);
+}
+
+// Stores four normalised values of a row: y itself, or (kSplit) its tf32
+// parts hi = tf32(y), lo = tf32(y - hi), the operand form of the tensor-core
+// GEMM (mamba_split_tf32's output for the same y).
+template <bool kSplit>
+__device__ __forceinline__ void store_norm4(float* y, float* hi, float* lo, const float4 v) {
+  if (!kSplit) {
+    *reinterpret_cast<float4*>(y) = v;
+    return;
+  }
+  const float4 h = make_float4(round_tf32(v.x), round_tf32(v.y), round_tf32(v.z), round_tf32(v.w));
+  *reinterpret_cast<float4*>(hi) = h;
+  *reinterpret_cast<float4*>(lo) = make_float4(round_tf32(v.x - h.x), round_tf32(v.y - h.y),
+                                               round_tf32(v.z - h.z), round_tf32(v.w - h.w));
+}
+
 // kVec: rows of cols % 4 == 0 floats with 16-byte aligned bases.
-template <bool kVec>
+// kSplit: y is not written; hi and lo (rows of ld floats, ld % 4 == 0)
+// receive the tf32 parts of each normalised value (kVec only).
+template <bool kVec, bool kSplit = false>
 __global__ void __launch_bounds__(kNormWarps * 32)
     rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
-                   float* __restrict__ y, int64_t rows, int cols, float eps) {
+                   float* __restrict__ y, int64_t rows, int cols, float eps,
+                   float* __restrict__ hi = nullptr, float* __restrict__ lo = nullptr,
+                   int64_t ld = 0) {
+  static_assert(kVec || !kSplit, "the split form stores float4s");
   pdl_enter();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t r = (int64_t)blockIdx.x * kNormWarps + warp;
   if (r >= rows) return;
   const float* xr = x + r * cols;
-  float* yr = y + r * cols;
+  float* yr = kSplit ? nullptr : y + r * cols;
+  float* hr = kSplit ? hi + r * ld : nullptr;
+  float* lr = kSplit ? lo + r * ld : nullptr;
   float ss = 0.f;
   if (kVec) {
     for (int c = lane * 4; c < cols; c += 128) {
@@ -90,8 +120,9 @@ __global__ void __launch_bounds__(kNormWarps * 32)
     for (int c = lane * 4; c < cols; c += 128) {
       const float4 v = __ldg(reinterpret_cast<const float4*>(xr + c));
       const float4 g = __ldg(reinterpret_cast<const float4*>(w + c));
-      *reinterpret_cast<float4*>(yr + c) =
-          make_float4(v.x * inv * g.x, v.y * inv * g.y, v.z * inv * g.z, v.w * inv * g.w);
+      store_norm4<kSplit>(yr + c, hr + c, lr + c,
+                          make_float4(v.x * inv * g.x, v.y * inv * g.y, v.z * inv * g.z,
+                                      v.w * inv * g.w));
     }
   } else {
     for (int c = lane; c < cols; c += 32) yr[c] = xr[c] * inv * w[c];
@@ -708,11 +739,45 @@ int mamba_rmsnorm(const float* x, const float* weight, float* y, int64_t rows, i
   const unsigned grid = (unsigned)((rows + kNormWarps - 1) / kNormWarps);
   const bool vec = cols % 4 == 0 && aligned16(x) && aligned16(weight) && aligned16(y);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  float* const none = nullptr;
   const cudaError_t e =
       vec ? launch_pdl(rmsnorm_kernel<true>, dim3(grid), dim3(kNormWarps * 32), 0, st, x, weight,
-                       y, rows, (int)cols, eps)
+                       y, rows, (int)cols, eps, none, none, (int64_t)0)
           : launch_pdl(rmsnorm_kernel<false>, dim3(grid), dim3(kNormWarps * 32), 0, st, x, weight,
-                       y, rows, (int)cols, eps);
+                       y, rows, (int)cols, eps, none, none, (int64_t)0);
+  if (e != cudaSuccess) return set_last_error(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
+  return MAMBA_SCAN_OK;
+}
+
+int mamba_rmsnorm_split_tf32(const float* x, const float* weight, int64_t rows, int64_t cols,
+                             float eps, float* hi, float* lo, int64_t ld, void* stream) {
+  using mamba_scan::set_last_error;
+  if (rows < 0 || cols <= 0 || cols > (1 << 20))
+    return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "rmsnorm_split_tf32: bad rows/cols");
+  if (rows == 0) return MAMBA_SCAN_OK;
+  if (!x || !weight || !hi || !lo)
+    return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "rmsnorm_split_tf32: NULL pointer");
+  if (cols % 4 != 0 || ld < cols || ld % 4 != 0 || !aligned16(x) || !aligned16(weight) ||
+      !aligned16(hi) || !aligned16(lo))
+    return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT,
+                          "rmsnorm_split_tf32: cols and ld must be multiples of 4 (ld >= cols) "
+                          "and every pointer 16-byte aligned");
+  {
+    const uintptr_t x0 = reinterpret_cast<uintptr_t>(x), n = (uintptr_t)rows * (uintptr_t)cols * 4;
+    const uintptr_t m = ((uintptr_t)(rows - 1) * (uintptr_t)ld + (uintptr_t)cols) * 4;
+    const uintptr_t h0 = reinterpret_cast<uintptr_t>(hi), l0 = reinterpret_cast<uintptr_t>(lo);
+    if ((x0 < h0 + m && h0 < x0 + n) || (x0 < l0 + m && l0 < x0 + n) ||
+        (h0 < l0 + m && l0 < h0 + m))
+      return set_last_error(MAMBA_SCAN_ERR_ALIASING,
+                            "rmsnorm_split_tf32: x, hi and lo must not overlap");
+  }
+  if (rows > ((int64_t)1 << 31) * kNormWarps)
+    return set_last_error(MAMBA_SCAN_ERR_INVALID_ARGUMENT, "rmsnorm_split_tf32: too many rows");
+  const unsigned grid = (unsigned)((rows + kNormWarps - 1) / kNormWarps);
+  float* const none = nullptr;
+  const cudaError_t e = launch_pdl(rmsnorm_kernel<true, true>, dim3(grid), dim3(kNormWarps * 32), 0,
+                                   static_cast<cudaStream_t>(stream), x, weight, none, rows,
+                                   (int)cols, eps, hi, lo, ld);
   if (e != cudaSuccess) return set_last_error(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
   return MAMBA_SCAN_OK;
 }

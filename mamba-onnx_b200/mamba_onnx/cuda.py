@@ -124,6 +124,9 @@ def library() -> ctypes.CDLL:
             [ctypes.c_void_p] * 2 + [ctypes.c_int64] * 5 + \
             [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
         lib.mamba_gemm_tf32x3_workspace_size.restype = ctypes.c_size_t
+        lib.mamba_rmsnorm_split_tf32.restype = ctypes.c_int
+        lib.mamba_rmsnorm_split_tf32.argtypes = [ctypes.c_void_p] * 2 + [ctypes.c_int64] * 2 + \
+            [ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p]
         lib.mamba_gemm_tf32x3_workspace_size.argtypes = [ctypes.c_int64] * 3
         _lib = lib
     return _lib
@@ -561,6 +564,11 @@ class SplitTF32:
     def ld(self) -> int:
         return self.hi.shape[1]
 
+    def row_block(self, start: int, count: int) -> "SplitTF32":
+        """Rows [start, start + count) as a SplitTF32 (views, no copy)."""
+        return SplitTF32(self.hi[start:start + count], self.lo[start:start + count], count,
+                         self.cols)
+
 
 def split_tf32(x, transpose: bool = False, out: SplitTF32 | None = None,
                stream=None) -> SplitTF32:
@@ -585,6 +593,27 @@ def split_tf32(x, transpose: bool = False, out: SplitTF32 | None = None,
                                     _ptr(out.lo), out.ld, st.cuda_stream)
     if rc != STATUS_OK:
         _raise(rc, "split_tf32")
+    return out
+
+
+def rmsnorm_split_tf32(x, weight, eps: float, stream=None) -> SplitTF32:
+    """rmsnorm(x, weight, eps) over the last dimension of a contiguous CUDA
+    float32 tensor, delivered as the GEMM operand split_tf32 would make of it
+    ([rows][cols], rows = all leading dimensions; mamba_rmsnorm_split_tf32).
+    cols must be a multiple of 4."""
+    import torch
+
+    cols = x.shape[-1]
+    _check("x", x, tuple(x.shape))
+    _check("weight", weight, (cols,))
+    rows = x.numel() // cols
+    out = SplitTF32(torch.empty((rows, cols), dtype=torch.float32, device=x.device),
+                    torch.empty((rows, cols), dtype=torch.float32, device=x.device), rows, cols)
+    st = stream if stream is not None else torch.cuda.current_stream(x.device)
+    rc = library().mamba_rmsnorm_split_tf32(_ptr(x), _ptr(weight), rows, cols, float(eps),
+                                            _ptr(out.hi), _ptr(out.lo), cols, st.cuda_stream)
+    if rc != STATUS_OK:
+        _raise(rc, "rmsnorm_split_tf32")
     return out
 
 

@@ -207,11 +207,21 @@ class MambaLayer(torch.nn.Module):
 
     def _in_proj(self, h):
         """rmsnorm(h) [B, L, d] -> in_proj output xz [B, 2D, L] (x rows, then z rows)."""
+        if _use_tc(h, h.shape[1]) and h.shape[-1] % 4 == 0:
+            # the norm writes the GEMM operand's tf32 parts directly
+            hs = cuda.rmsnorm_split_tf32(h.contiguous(), self.norm_weight.detach(),
+                                         self.cfg.rms_eps)
+            w = self._in_split.get(self.in_proj_weight)
+            L = h.shape[1]
+            xz = torch.empty(h.shape[0], w.rows, L, device=h.device)
+            for b in range(h.shape[0]):  # xz[b] [2D, L] = W hn[b]^T
+                cuda.gemm_tf32x3(w, hs.row_block(b * L, L), xz[b])
+            return xz
         hn = self._norm(h)
         if _use_tc(h, h.shape[1]):
             w = self._in_split.get(self.in_proj_weight)
             xz = torch.empty(h.shape[0], w.rows, h.shape[1], device=h.device)
-            for b in range(h.shape[0]):  # xz[b] [2D, L] = W hn[b]^T
+            for b in range(h.shape[0]):
                 cuda.gemm_tf32x3(w, cuda.split_tf32(hn[b]), xz[b])
             return xz
         if h.shape[0] == 1:
@@ -336,6 +346,15 @@ class MambaLM(torch.nn.Module):
     # ---------------------------------------------------------------- forward
 
     def _head(self, h):
+        if _use_tc(h, h.shape[1]) and h.shape[-1] % 4 == 0:
+            hs = cuda.rmsnorm_split_tf32(h.contiguous(), self.norm_f_weight.detach(),
+                                         self.cfg.rms_eps)
+            e = self._emb_split.get(self.embedding)
+            L = h.shape[1]
+            logits = torch.empty(h.shape[0], L, e.rows, device=h.device)
+            for b in range(h.shape[0]):  # logits[b] [L, V] = hn[b] E^T
+                cuda.gemm_tf32x3(hs.row_block(b * L, L), e, logits[b])
+            return logits
         h = rms_norm(h, self.norm_f_weight, self.cfg.rms_eps)
         if _use_tc(h, h.shape[1]):
             e = self._emb_split.get(self.embedding)

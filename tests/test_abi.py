@@ -144,6 +144,20 @@ def test_gemm_and_split_validate_before_launch():
     assert gemm(ldc_m=0) == 1
 
 
+def test_rmsnorm_split_validates_before_launch():
+    lib = cuda.library()
+    f = 0x100000
+
+    def call(x=f, w=2 * f, rows=4, cols=8, hi=3 * f, lo=4 * f, ld=8):
+        return lib.mamba_rmsnorm_split_tf32(x, w, rows, cols, 1e-5, hi, lo, ld, None)
+
+    assert call(rows=0) == 0
+    assert call(cols=6, ld=8) == 1 and call(ld=4) == 1 and call(ld=10) == 1
+    assert call(hi=3 * f + 4) == 1 and b"aligned" in lib.mamba_scan_last_error()
+    assert call(lo=None) == 1
+    assert call(hi=f + 64) == 4 and call(lo=3 * f + 16) == 4
+
+
 def test_gemm_split_workspace_validates_before_launch():
     """mamba_gemm_tf32x3_ws: the split of K is planned on the host; a short,
     misaligned or overlapping workspace is rejected before any launch."""

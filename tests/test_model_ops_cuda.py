@@ -37,6 +37,20 @@ def test_rmsnorm_unaligned_input_takes_the_scalar_path():
                                rtol=1e-5, atol=1e-6)
 
 
+@pytest.mark.parametrize("shape", [(1, 1024, 768), (3, 7, 64), (5, 4)])
+def test_rmsnorm_split_equals_rmsnorm_then_split(shape):
+    """The fused norm + tf32 split writes exactly split_tf32(rmsnorm(x))."""
+    g = torch.Generator(device="cuda").manual_seed(3)
+    x = torch.randn(*shape, device="cuda", generator=g) * 3
+    w = torch.randn(shape[-1], device="cuda", generator=g)
+    got = cuda.rmsnorm_split_tf32(x, w, 1e-5)
+    want = cuda.split_tf32(cuda.rmsnorm(x, w, 1e-5).reshape(-1, shape[-1]))
+    assert (got.rows, got.cols) == (want.rows, want.cols)
+    assert torch.equal(got.hi, want.hi[:, :shape[-1]]) and torch.equal(got.lo, want.lo[:, :shape[-1]])
+    with pytest.raises(RuntimeError, match="multiples of 4"):
+        cuda.rmsnorm_split_tf32(torch.randn(2, 6, device="cuda"), torch.randn(6, device="cuda"), 1e-5)
+
+
 def _torch_conv_silu(x, w, b):
     K, L = w.shape[-1], x.shape[-1]
     return F.silu(F.conv1d(x, w, b, padding=K - 1, groups=x.shape[1])[..., :L])
