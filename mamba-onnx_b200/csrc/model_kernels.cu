@@ -359,14 +359,18 @@ __global__ void __launch_bounds__(kSsmThreads)
 
 constexpr int kXpCluster = 8;    // CTAs per token block, each 1/8 of d_inner
 constexpr int kXpTokens = 32;    // tokens per block: 8 groups of 4
-constexpr int kXpThreads = 256;  // 8 token groups x 32 output groups
+constexpr int kXpThreads = 256;  // 8 token groups x 32 groups of 4 outputs
 constexpr int kXpDChunk = 96;    // d_inner rows staged per step (2 steps at d_inner 1536)
 constexpr int kXpMaxOut = 128;   // rank + 2 * dstate
-constexpr int kXpRow = kXpMaxOut + 1;  // padded smem rows (conflict-free column writes)
+constexpr int kXpRow = kXpMaxOut + 1;  // padded rows of the partial tile
+// Row stride of the staged weights: 16-byte aligned rows for the float4
+// reads, and 132 = 4 (mod 32) so the float4 stores of 32 consecutive rows
+// spread over all banks.
+constexpr int kXpWRow = kXpMaxOut + 4;
 
 struct XpStage {
   float x[kXpDChunk][kXpTokens];  // x[d][t] of the chunk
-  float w[kXpDChunk][kXpRow];     // W_x[j][d], transposed to [d][j]
+  float w[kXpDChunk][kXpWRow];    // W_x[j][d], transposed to [d][j]
 };
 union XpSmem {
   XpStage stage;
@@ -382,11 +386,15 @@ static_assert(kXpDtMaxRank * (kXpDtRow + kXpDChunk) * 4 <= sizeof(XpSmem), "fuse
 constexpr size_t kXpDtlBytes = (size_t)kXpMaxOut * (kXpTokens / kXpCluster) * 4;
 constexpr size_t kXpSmemBytes = sizeof(XpSmem) + kXpDtlBytes;
 
-// kOut = outputs per thread (P <= 32 kOut): 3 for Mamba-130m's P = 80.
+// Thread (og, tg) = (tid / 8, tid % 8) sums outputs 4 og .. 4 og + 3 of
+// tokens 4 tg .. 4 tg + 3 over its CTA's d_inner range: per d one float4 of
+// x and one of W, and 8 packed FMAs over token pairs (each output's sum runs
+// over d in order, as a scalar loop would). Warps whose outputs all lie past
+// P (rank + 2 * dstate) only stage.
 // kDelta: dt_proj fused, delta[b, d, t] = sum_k w_dt[d, k] dt[b, t, k]
 // written instead of dt (rank <= kXpDtMaxRank): each CTA of the cluster
 // forms delta for its own d_inner range and the cluster's 32 tokens.
-template <int kOut, bool kDelta>
+template <bool kDelta>
 __global__ void __cluster_dims__(kXpCluster, 1, 1) __launch_bounds__(kXpThreads, 2)
     xproj_kernel(const float* __restrict__ x, const float* __restrict__ w, float* __restrict__ dt,
                  float* __restrict__ Bm, float* __restrict__ Cm, int dim, int seqlen, int rank,
@@ -404,20 +412,21 @@ __global__ void __cluster_dims__(kXpCluster, 1, 1) __launch_bounds__(kXpThreads,
   const int d_lo = min(dim, crank * per), d_hi = min(dim, d_lo + per);
   const float* xb = x + (int64_t)b * dim * seqlen;
   const int tid = threadIdx.x, tg = tid & 7, og = tid >> 3;
+  const bool computes = 4 * (og & ~3) < P;  // warp-uniform: the warp's 16 outputs start below P
 
-  float acc[4][kOut];
+  float2 acc[2][4];  // [token pair][output]: .x token 4 tg + 2 p, .y the next
 #pragma unroll
-  for (int a = 0; a < 4; ++a)
+  for (int p2 = 0; p2 < 2; ++p2)
 #pragma unroll
-    for (int k = 0; k < kOut; ++k) acc[a][k] = 0.f;
+    for (int o = 0; o < 4; ++o) acc[p2][o] = make_float2(0.f, 0.f);
 
   // Loads of a 96-row chunk go to registers first, all issued before any is
-  // stored (x: 12 per thread, rows of 32 tokens; W: 12 kOut per thread, rows
-  // of 96 d_inner values, zeros for the unused columns P..32 kOut): one
-  // load round trip per chunk.
-  constexpr int kXq = kXpDChunk * kXpTokens / kXpThreads;       // 12
-  constexpr int kWq = kXpDChunk * 32 * kOut / kXpThreads;       // 12 kOut
-  float xr[kXq], wr[kWq];
+  // stored (x: 12 per thread, rows of 32 tokens; W: 12 x 4 per thread, four
+  // outputs of one d_inner row, zeros past P): one load round trip per chunk.
+  constexpr int kXq = kXpDChunk * kXpTokens / kXpThreads;         // 12
+  constexpr int kWq = kXpDChunk * (kXpMaxOut / 4) / kXpThreads;   // 12
+  float xr[kXq];
+  float4 wr[kWq];
   auto fetch = [&](int dc) {
 #pragma unroll
     for (int q = 0; q < kXq; ++q) {
@@ -426,8 +435,13 @@ __global__ void __cluster_dims__(kXpCluster, 1, 1) __launch_bounds__(kXpThreads,
     }
 #pragma unroll
     for (int q = 0; q < kWq; ++q) {
-      const int i = tid + kXpThreads * q, j = i / kXpDChunk, d = dc + i % kXpDChunk;
-      wr[q] = (j < P && d < d_hi) ? __ldg(w + (int64_t)j * dim + d) : 0.f;
+      const int i = tid + kXpThreads * q, j = 4 * (i / kXpDChunk), d = dc + i % kXpDChunk;
+      const bool dok = d < d_hi;
+      const float* wc = w + (int64_t)j * dim + d;
+      wr[q] = make_float4((dok && j < P) ? __ldg(wc) : 0.f,
+                          (dok && j + 1 < P) ? __ldg(wc + dim) : 0.f,
+                          (dok && j + 2 < P) ? __ldg(wc + 2 * dim) : 0.f,
+                          (dok && j + 3 < P) ? __ldg(wc + 3 * dim) : 0.f);
     }
   };
   for (int dc = d_lo; dc < d_hi; dc += kXpDChunk) {
@@ -438,28 +452,34 @@ __global__ void __cluster_dims__(kXpCluster, 1, 1) __launch_bounds__(kXpThreads,
 #pragma unroll
     for (int q = 0; q < kWq; ++q) {
       const int i = tid + kXpThreads * q;
-      sm.stage.w[i % kXpDChunk][i / kXpDChunk] = wr[q];
+      *reinterpret_cast<float4*>(&sm.stage.w[i % kXpDChunk][4 * (i / kXpDChunk)]) = wr[q];
     }
     __syncthreads();
     const int n = min(kXpDChunk, d_hi - dc);
+    if (computes) {
 #pragma unroll 4
-    for (int dd = 0; dd < n; ++dd) {
-      const float4 xv = *reinterpret_cast<const float4*>(&sm.stage.x[dd][4 * tg]);
+      for (int dd = 0; dd < n; ++dd) {
+        const float4 xv = *reinterpret_cast<const float4*>(&sm.stage.x[dd][4 * tg]);
+        const float4 wv = *reinterpret_cast<const float4*>(&sm.stage.w[dd][4 * og]);
+        const float2 x01 = make_float2(xv.x, xv.y), x23 = make_float2(xv.z, xv.w);
+        const float wo[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
-      for (int k = 0; k < kOut; ++k) {
-        const float wv = sm.stage.w[dd][og + 32 * k];  // columns >= P: zeros, unused sums
-        acc[0][k] = fmaf(xv.x, wv, acc[0][k]);
-        acc[1][k] = fmaf(xv.y, wv, acc[1][k]);
-        acc[2][k] = fmaf(xv.z, wv, acc[2][k]);
-        acc[3][k] = fmaf(xv.w, wv, acc[3][k]);
+        for (int o = 0; o < 4; ++o) {
+          const float2 w2 = make_float2(wo[o], wo[o]);
+          acc[0][o] = mamba_scan::fma2(x01, w2, acc[0][o]);
+          acc[1][o] = mamba_scan::fma2(x23, w2, acc[1][o]);
+        }
       }
     }
   }
   __syncthreads();  // the staging area becomes the partial tile
 #pragma unroll
-  for (int a = 0; a < 4; ++a)
+  for (int p2 = 0; p2 < 2; ++p2)
 #pragma unroll
-    for (int k = 0; k < kOut; ++k) sm.part[4 * tg + a][og + 32 * k] = acc[a][k];
+    for (int o = 0; o < 4; ++o) {
+      sm.part[4 * tg + 2 * p2][4 * og + o] = acc[p2][o].x;
+      sm.part[4 * tg + 2 * p2 + 1][4 * og + o] = acc[p2][o].y;
+    }
   cluster.sync();  // every CTA's partial tile is complete and visible
   // this CTA completes token rows [4 crank, 4 crank + 4): the 8 partials
   // added in rank order
@@ -597,25 +617,24 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-template <int kOut>
 cudaError_t launch_xproj(dim3 grid, cudaStream_t st, const float* x, const float* w, float* dt,
                          float* Bm, float* Cm, int dim, int seqlen, int rank, int dstate,
                          const float* w_dt = nullptr, float* delta = nullptr) {
   static std::once_flag once;
   static cudaError_t attr = cudaSuccess;
   std::call_once(once, [] {
-    attr = cudaFuncSetAttribute(xproj_kernel<kOut, false>,
-                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kXpSmemBytes);
+    attr = cudaFuncSetAttribute(xproj_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)kXpSmemBytes);
     if (attr == cudaSuccess)
-      attr = cudaFuncSetAttribute(xproj_kernel<kOut, true>,
-                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kXpSmemBytes);
+      attr = cudaFuncSetAttribute(xproj_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)kXpSmemBytes);
   });
   if (attr != cudaSuccess) return attr;
   if (delta != nullptr)
-    return launch_pdl(xproj_kernel<kOut, true>, grid, dim3(kXpThreads), kXpSmemBytes, st, x, w,
-                      dt, Bm, Cm, dim, seqlen, rank, dstate, w_dt, delta);
-  return launch_pdl(xproj_kernel<kOut, false>, grid, dim3(kXpThreads), kXpSmemBytes, st, x, w, dt,
-                    Bm, Cm, dim, seqlen, rank, dstate, w_dt, delta);
+    return launch_pdl(xproj_kernel<true>, grid, dim3(kXpThreads), kXpSmemBytes, st, x, w, dt, Bm,
+                      Cm, dim, seqlen, rank, dstate, w_dt, delta);
+  return launch_pdl(xproj_kernel<false>, grid, dim3(kXpThreads), kXpSmemBytes, st, x, w, dt, Bm,
+                    Cm, dim, seqlen, rank, dstate, w_dt, delta);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -855,12 +874,8 @@ int mamba_x_proj(const float* x, const float* weight, float* dt, float* B, float
     return MAMBA_SCAN_OK;
   }
   const dim3 grid((unsigned)((seqlen + kXpTokens - 1) / kXpTokens * kXpCluster), (unsigned)batch);
-  const cudaError_t e =
-      (rank + 2 * dstate <= 32 * 3)
-          ? launch_xproj<3>(grid, st, x, weight, dt, B, C, (int)dim, (int)seqlen, (int)rank,
-                            (int)dstate)
-          : launch_xproj<4>(grid, st, x, weight, dt, B, C, (int)dim, (int)seqlen, (int)rank,
-                            (int)dstate);
+  const cudaError_t e = launch_xproj(grid, st, x, weight, dt, B, C, (int)dim, (int)seqlen,
+                                     (int)rank, (int)dstate);
   if (e != cudaSuccess) return set_last_error(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
   return MAMBA_SCAN_OK;
 }
@@ -894,12 +909,8 @@ int mamba_x_proj_delta(const float* x, const float* weight, const float* dt_weig
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const dim3 grid((unsigned)((seqlen + kXpTokens - 1) / kXpTokens * kXpCluster), (unsigned)batch);
-  const cudaError_t e =
-      (rank + 2 * dstate <= 32 * 3)
-          ? launch_xproj<3>(grid, st, x, weight, nullptr, B, C, (int)dim, (int)seqlen, (int)rank,
-                            (int)dstate, dt_weight, delta)
-          : launch_xproj<4>(grid, st, x, weight, nullptr, B, C, (int)dim, (int)seqlen, (int)rank,
-                            (int)dstate, dt_weight, delta);
+  const cudaError_t e = launch_xproj(grid, st, x, weight, nullptr, B, C, (int)dim, (int)seqlen,
+                                     (int)rank, (int)dstate, dt_weight, delta);
   if (e != cudaSuccess) return set_last_error(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
   return MAMBA_SCAN_OK;
 }
