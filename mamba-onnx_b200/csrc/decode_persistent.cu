@@ -113,7 +113,13 @@ __device__ __forceinline__ void barrier_arrive(unsigned int* ctl) {
 }
 
 // Wait until every CTA has arrived at barrier k; false when the launch is
-// being abandoned (a wait timed out here or in another CTA).
+// being abandoned (a wait timed out here or in another CTA). Thread 0 polls
+// the counter and the abort flag with one 8-byte acquire load (ctl is the
+// 16-byte aligned scratch base). No fence follows: the acquire load that sees
+// the count synchronises with every CTA's release reduction, and the
+// __syncthreads after it orders the other threads' reads behind it; every
+// read of another CTA's results goes to L2 (__ldcg), never to a stale L1
+// line. (A __threadfence here cost 0.4 us per barrier, 39 us per token.)
 __device__ __noinline__ bool barrier_wait(unsigned int* ctl, unsigned int k,
                                           uint64_t limit_ns = kBarrierLimitNs) {
   __shared__ int ok_s;
@@ -123,8 +129,10 @@ __device__ __noinline__ bool barrier_wait(unsigned int* ctl, unsigned int k,
     if (ld_acquire(ctl) < target) {
       const uint64_t start = mamba_scan::globaltimer_ns();
       for (uint32_t spins = 0;; ++spins) {
-        if (ld_acquire(ctl) >= target) break;
-        if (ld_acquire(ctl + 1) != 0u || spins >= (1u << 28)) {
+        unsigned long long both;
+        asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(both) : "l"(ctl) : "memory");
+        if ((unsigned int)both >= target) break;
+        if ((unsigned int)(both >> 32) != 0u || spins >= (1u << 28)) {
           ok = 0;
           break;
         }
@@ -136,7 +144,6 @@ __device__ __noinline__ bool barrier_wait(unsigned int* ctl, unsigned int k,
         }
       }
     }
-    __threadfence();
     ok_s = ok;
   }
   __syncthreads();
