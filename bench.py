@@ -533,8 +533,8 @@ MODEL_METRIC, MODEL_UNIT = "Mamba-130m forward tokens/s", "tokens/s"
 MODEL_WORKLOAD = ("Mamba-130m forward (24 blocks, d_model 768, d_inner 1536, d_state 16, "
                   "vocab 50280), fp32, batch 1 x seqlen 1024 per GPU, every selective scan on "
                   "SelectiveScanFusedExact; in_proj, out_proj and the LM head on the "
-                  "tensor-core 3xTF32 GEMM (fp32-accurate), x_proj on this package's fp32 "
-                  "kernel, dt_proj on cuBLAS fp32")
+                  "tensor-core 3xTF32 GEMM (fp32-accurate), x_proj and dt_proj on this "
+                  "package's fp32 kernels")
 
 
 def model_cpu_sample(n_threads, budget_s=30.0):
@@ -603,6 +603,7 @@ def run_model(args):
     import torch.distributed as dist
 
     from mamba_onnx import cuda
+    from mamba_onnx import model as M
     from mamba_onnx.model import SCAN_OP, MambaLM, mamba_130m
 
     torch.cuda.set_device(local)
@@ -733,11 +734,12 @@ def run_model(args):
                     "d2h_bytes_per_step": host_last.numel() * 4, "ms_per_step": e2e_ms,
                     "path": "pinned token ids -> graph replay -> last-position logits to host"},
             # this package's kernels per forward: per block the RMSNorm that
-            # writes in_proj's tf32 operand, in_proj, conv + SiLU, x_proj, the
-            # scan, y's tf32 split, out_proj (and its split-K reduction);
-            # then the final RMSNorm (to the LM head's operand) and the LM head
-            "gpu_launches": (model.cfg.n_layer * (6 + launches_per_scan + out_proj_reduce) + 2)
-            * args.steps,
+            # writes in_proj's tf32 operand, in_proj, conv + SiLU, x_proj,
+            # dt_proj (unless on cuBLAS), the scan, y's tf32 split, out_proj
+            # (and its split-K reduction); then the final RMSNorm (to the LM
+            # head's operand) and the LM head
+            "gpu_launches": (model.cfg.n_layer * (6 + (M.DT_PROJ == "kernel") + launches_per_scan
+                                                  + out_proj_reduce) + 2) * args.steps,
             "scan_ms_per_step": scan_ms,
             "ort_entry": {"ms_per_step": ort_ms, "value": world * B * L / (ort_ms * 1e-3),
                           "unit": MODEL_UNIT,

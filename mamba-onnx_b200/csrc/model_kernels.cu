@@ -655,13 +655,25 @@ bool overlap(const void* a, size_t abytes, const void* b, size_t bbytes) {
 // reads its 4 d and 8 l values as float4s; each thread keeps 4 x 8 outputs
 // (packed FFMA2 over l pairs) summed in k order, and stores float4 runs
 // along l. The weight tile is loaded before waiting for the previous kernel.
+//
+// Both operands are [rows][rank] in memory (k contiguous): kVec (rank % 4 ==
+// 0, 16-byte aligned bases) loads them as float4 runs along k, coalesced,
+// and scatters each into 4 k-rows of the tile. Columns are swizzled in
+// groups of 4 (group g of k-row k sits at g ^ ((k / 4) % 8)), so those
+// scattered stores spread over the banks while the float4 reads of 4
+// consecutive columns stay whole and aligned.
 constexpr int kDtBM = 64, kDtBN = 64, kDtBK = 64, kDtThreads = 128;
 
+__device__ __forceinline__ int dt_swz(int c, int k) {
+  return ((((c >> 2) ^ (k >> 2)) & 7) | ((c >> 2) & 8)) << 2 | (c & 3);
+}
+
+template <bool kVec>
 __global__ void __launch_bounds__(kDtThreads)
     dt_proj_kernel(const float* __restrict__ dt, const float* __restrict__ w,
                    float* __restrict__ delta, int dim, int seqlen, int rank) {
   __shared__ __align__(16) float ws[kDtBK][kDtBM];
-  __shared__ __align__(16) float xs[kDtBK][kDtBN + 4];
+  __shared__ __align__(16) float xs[kDtBK][kDtBN];
   const int tid = threadIdx.x;
   const int b = blockIdx.z, d0 = blockIdx.y * kDtBM, l0 = blockIdx.x * kDtBN;
   const float* dtb = dt + (int64_t)b * seqlen * rank;
@@ -671,37 +683,68 @@ __global__ void __launch_bounds__(kDtThreads)
   for (int i = 0; i < 4; ++i)
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[i][j] = make_float2(0.f, 0.f);
-  // Loader roles: element i = tid + 128 j of a 64 x kn tile is (row i % 64,
-  // k = i / 64); every load of a tile is issued before any is stored.
+  // kVec loaders: float4 q = tid + 128 j of a 64 x 64 tile is (row q / 16,
+  // k = 4 (q % 16)); otherwise element i = tid + 128 j is (row i % 64,
+  // k = i / 64). Every load of a tile is issued before any is stored.
   constexpr int kLd = kDtBM * kDtBK / kDtThreads;  // 32 elements per thread and tile
-  const int lrow = tid & 63, lk = tid >> 6;
+  constexpr int kLd4 = kLd / 4;
   float r[kLd];
+  // a tile of a [rows][rank] operand (rows from row0, K step k0, kn wide)
+  // into registers
+  auto load = [&](const float* src, int row0, int nrows, int k0, int kn) {
+    if (kVec) {
+#pragma unroll
+      for (int j = 0; j < kLd4; ++j) {
+        const int q = tid + kDtThreads * j, row = q >> 4, k = 4 * (q & 15);
+        const float4 v = (row0 + row < nrows && k < kn)
+                             ? __ldg(reinterpret_cast<const float4*>(
+                                   src + (int64_t)(row0 + row) * rank + k0 + k))
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+        r[4 * j] = v.x;
+        r[4 * j + 1] = v.y;
+        r[4 * j + 2] = v.z;
+        r[4 * j + 3] = v.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < kLd; ++j) {
+        const int row = tid & 63, k = (tid >> 6) + 2 * j;
+        r[j] = (row0 + row < nrows && k < kn) ? src[(int64_t)(row0 + row) * rank + k0 + k] : 0.f;
+      }
+    }
+  };
+  auto store = [&](float (*tile)[64]) {
+    if (kVec) {
+#pragma unroll
+      for (int j = 0; j < kLd4; ++j) {
+        const int q = tid + kDtThreads * j, row = q >> 4, k = 4 * (q & 15);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) tile[k + e][dt_swz(row, k + e)] = r[4 * j + e];
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < kLd; ++j) {
+        const int row = tid & 63, k = (tid >> 6) + 2 * j;
+        tile[k][dt_swz(row, k)] = r[j];
+      }
+    }
+  };
   for (int k0 = 0; k0 < rank; k0 += kDtBK) {
     const int kn = min(kDtBK, rank - k0);
     if (k0 > 0) __syncthreads();  // the previous K step has been read
-#pragma unroll
-    for (int j = 0; j < kLd; ++j) {
-      const int k = lk + 2 * j;
-      r[j] = (d0 + lrow < dim && k < kn) ? __ldg(w + (int64_t)(d0 + lrow) * rank + k0 + k) : 0.f;
-    }
-#pragma unroll
-    for (int j = 0; j < kLd; ++j) ws[lk + 2 * j][lrow] = r[j];
+    load(w, d0, dim, k0, kn);
+    store(ws);
     // dt is the previous kernel's output (x_proj): wait for it (a no-op
     // unless launched as a programmatic dependent launch)
     if (k0 == 0) pdl_enter();
-#pragma unroll
-    for (int j = 0; j < kLd; ++j) {
-      const int k = lk + 2 * j;
-      r[j] = (l0 + lrow < seqlen && k < kn) ? dtb[(int64_t)(l0 + lrow) * rank + k0 + k] : 0.f;
-    }
-#pragma unroll
-    for (int j = 0; j < kLd; ++j) xs[lk + 2 * j][lrow] = r[j];
+    load(dtb, l0, seqlen, k0, kn);
+    store(xs);
     __syncthreads();
 #pragma unroll 8
     for (int k = 0; k < kn; ++k) {
-      const float4 wv = *reinterpret_cast<const float4*>(&ws[k][4 * ty]);
-      const float4 x0 = *reinterpret_cast<const float4*>(&xs[k][4 * tx]);
-      const float4 x1 = *reinterpret_cast<const float4*>(&xs[k][32 + 4 * tx]);
+      const float4 wv = *reinterpret_cast<const float4*>(&ws[k][dt_swz(4 * ty, k)]);
+      const float4 x0 = *reinterpret_cast<const float4*>(&xs[k][dt_swz(4 * tx, k)]);
+      const float4 x1 = *reinterpret_cast<const float4*>(&xs[k][dt_swz(32 + 4 * tx, k)]);
       const float wi[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -932,8 +975,12 @@ int mamba_dt_proj(const float* dt, const float* weight, float* delta, int64_t ba
     return set_last_error(MAMBA_SCAN_ERR_ALIASING, "dt_proj: delta overlaps an input");
   const dim3 grid((unsigned)((seqlen + kDtBN - 1) / kDtBN), (unsigned)((dim + kDtBM - 1) / kDtBM),
                   (unsigned)batch);
-  dt_proj_kernel<<<grid, kDtThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      dt, weight, delta, (int)dim, (int)seqlen, (int)rank);
+  if (rank % 4 == 0 && aligned16(dt) && aligned16(weight))
+    dt_proj_kernel<true><<<grid, kDtThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+        dt, weight, delta, (int)dim, (int)seqlen, (int)rank);
+  else
+    dt_proj_kernel<false><<<grid, kDtThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+        dt, weight, delta, (int)dim, (int)seqlen, (int)rank);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_last_error(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
   return MAMBA_SCAN_OK;

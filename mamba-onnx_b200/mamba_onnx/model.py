@@ -19,9 +19,10 @@ GEMMs instead); single-token steps use torch's fp32 GEMMs for those
 projections. x_proj, whose 80-wide output is too narrow to fill the GPU with
 GEMM tiles, runs on this package's fp32 kernel (d_inner split over a cluster
 of 8 CTAs, or one warp per output when decoding; dt, B and C written apart),
-and dt_proj runs fused behind it (each CTA of the cluster forms the scan's
-[B, D, L] delta for its own d_inner rows from the cluster's dt; ``DT_PROJ``
-selects a standalone kernel or torch's fp32 GEMM instead). ``forward`` runs a whole
+and dt_proj on this package's K = dt_rank kernel, which writes the scan's
+[B, D, L] delta (``DT_PROJ`` selects it fused behind x_proj, each CTA of the
+cluster forming delta for its own d_inner rows, or torch's fp32 GEMM
+instead). ``forward`` runs a whole
 sequence; ``step`` decodes one
 token from a ``DecodeState`` (the convolution window and the 16 scan states
 per channel), which the scan carries in through ``h0`` and out through
@@ -44,9 +45,9 @@ SCAN_OP = "SelectiveScanFusedExact"
 # d_model <= 1024, d_inner <= 2048, dt_rank <= 64, d_conv <= 4, else the
 # chain) or the chain of per-block kernels ("chain"); both give the same values
 DECODE = "persistent"
-# dt_proj on CUDA: fused behind x_proj ("fused", dt_rank <= 96; else "kernel"),
-# this package's standalone kernel ("kernel") or torch's fp32 GEMM ("cublas")
-DT_PROJ = "cublas"
+# dt_proj on CUDA: this package's standalone kernel ("kernel"), fused behind
+# x_proj ("fused", dt_rank <= 96; else "kernel") or torch's fp32 GEMM ("cublas")
+DT_PROJ = "kernel"
 
 
 @dataclass(frozen=True)
