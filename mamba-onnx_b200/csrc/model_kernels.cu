@@ -178,6 +178,37 @@ __global__ void __launch_bounds__(kConvThreads)
   }
 }
 
+// The same for the width-4 convolution of Mamba models on 16-byte aligned
+// rows with seqlen % 4 == 0: CTA (row, blockIdx.y) covers 1024 steps of one
+// (b, d) row, each thread reading its inputs as two float4s (steps t0-4.. and
+// t0..) and the row's 4 weights as one; the same sums in the same order.
+__global__ void __launch_bounds__(kConvThreads)
+    conv4_silu_kernel(const float* __restrict__ x, int64_t x_bstride,
+                      const float* __restrict__ w, const float* __restrict__ bias,
+                      float* __restrict__ y, unsigned dim, int64_t seqlen) {
+  pdl_enter();
+  const int64_t t0 = ((int64_t)blockIdx.y * kConvThreads + threadIdx.x) * 4;
+  if (t0 >= seqlen) return;
+  const unsigned row = blockIdx.x, b = row / dim, d = row - b * dim;  // row = b * dim + d
+  const float* xr = x + (int64_t)b * x_bstride + (int64_t)d * seqlen;
+  const float4 cur = __ldg(reinterpret_cast<const float4*>(xr + t0));
+  const float4 prev = t0 > 0 ? __ldg(reinterpret_cast<const float4*>(xr + t0 - 4))
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+  const float win[7] = {prev.y, prev.z, prev.w, cur.x, cur.y, cur.z, cur.w};  // t0-3 .. t0+3
+  const float4 w4 = __ldg(reinterpret_cast<const float4*>(w + (int64_t)d * 4));
+  const float wk[4] = {w4.x, w4.y, w4.z, w4.w};
+  const float bd = bias ? __ldg(bias + d) : 0.f;
+  float o[4];
+#pragma unroll
+  for (int s = 0; s < 4; ++s) {
+    float acc = bd;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) acc = fmaf(wk[k], win[s + k], acc);
+    o[s] = silu_exact(acc);
+  }
+  *reinterpret_cast<float4*>(y + (int64_t)row * seqlen + t0) = make_float4(o[0], o[1], o[2], o[3]);
+}
+
 // ------------------------------------------------------ convolution step
 
 // One decoding step of the causal convolution, one thread per (b, d): the
@@ -871,6 +902,16 @@ int mamba_causal_conv1d_silu(const float* x, int64_t x_batch_stride, const float
   const unsigned grid = (unsigned)((n_items + kConvThreads - 1) / kConvThreads);
   const bool vec = seqlen % 4 == 0 && x_batch_stride % 4 == 0 && aligned16(x) && aligned16(y);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t t_blocks = (blocks_per_row + kConvThreads - 1) / kConvThreads;
+  if (vec && width == 4 && aligned16(weight) && batch * dim < ((int64_t)1 << 31) &&
+      t_blocks <= 65535) {
+    const cudaError_t e =
+        launch_pdl(conv4_silu_kernel, dim3((unsigned)(batch * dim), (unsigned)t_blocks),
+                   dim3(kConvThreads), 0, st, x, x_batch_stride, weight, bias, y, (unsigned)dim,
+                   seqlen);
+    if (e != cudaSuccess) return set_last_error(MAMBA_SCAN_ERR_CUDA, cudaGetErrorString(e));
+    return MAMBA_SCAN_OK;
+  }
   const cudaError_t e =
       vec ? launch_pdl(conv_silu_kernel<true>, dim3(grid), dim3(kConvThreads), 0, st, x,
                        x_batch_stride, weight, bias, y, dim, seqlen, blocks_per_row, n_items,

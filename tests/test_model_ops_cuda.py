@@ -58,6 +58,7 @@ def _torch_conv_silu(x, w, b):
 
 @pytest.mark.parametrize("batch,dim,seqlen,width", [
     (1, 1536, 1024, 4),  # Mamba-130m layer
+    (2, 48, 2052, 4),    # width 4 on float4 rows: several 1024-step blocks, a partial last one
     (2, 100, 37, 4),     # ragged sequence: scalar stores
     (3, 17, 64, 1), (1, 8, 5, 8), (2, 33, 200, 3), (1, 4, 1, 4),
 ])
