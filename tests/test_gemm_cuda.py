@@ -56,6 +56,10 @@ CASES = [
     (1024, 3500, 768, True, False),
     # few rows, many columns: single CTAs with 192-column tiles
     (64, 19008, 40, False, False),
+    # several waves of 256 x 256 pair tiles: ragged M, N, K; row-major C with
+    # C_in, column-major C
+    (1000, 20000, 100, False, True),
+    (700, 15000, 64, True, False),
 ]
 
 
