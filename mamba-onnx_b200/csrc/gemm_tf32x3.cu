@@ -46,15 +46,14 @@ using mamba_scan::smem_u32;
 
 constexpr int BM = 128, BK = 32;  // BK fp32 = 128 bytes: one swizzled row
 
-// Tile configurations: 128 x 64 with a 4-stage ring (48 KB per stage),
-// 128 x 128 with 3 stages (64 KB), 128 x 192 with 2 stages (80 KB). The host
-// picks the width with the fewest waves x (128 + BN), the operand bytes a
-// CTA streams per K block being (2 * 128 + 2 * BN) x 32 x 4: in_proj (192
-// tiles of 128 on 148 SMs) takes 144 tiles of 192 (55.8 -> 43.8 us),
-// out_proj (48 tiles of 128) 96 tiles of 64 (37.4 -> 35.5 us); the LM head
-// measured the same at 192 and 128 (649 and 637-660 us). A K block costs a
-// CTA 0.7-1.2 us whatever the width: TMA delivery per SM, not the bytes of
-// the whole GPU, sets it.
+// Single-CTA tile configurations: 128 x 64 with a 4-stage ring (48 KB per
+// stage), 128 x 128 with 3 stages (64 KB), 128 x 192 with 2 stages (80 KB).
+// The host picks the width with the fewest waves x (128 + BN), the operand
+// rows a CTA streams per K block being 2 * 128 + 2 * BN, then CTA pairs
+// (further down) when they cost no more; products with few output tiles
+// split K (plan_gemm). Per SM and K block the time goes to moving operands
+// through shared memory (TMA writes in, every MMA reading its A and whole B
+// slices out) as much as to the MMAs themselves.
 //
 // Warps 0..kAccWarps-1 accumulate and store: warp w owns TMEM lanes
 // 32(w%4)..+31 (tile rows) and columns [64(w/4), 64(w/4) + 64), so two or
