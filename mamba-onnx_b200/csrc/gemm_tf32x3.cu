@@ -430,7 +430,7 @@ __global__ void __launch_bounds__(C::kThreads, 1)
 // tensor cores of the pair read both halves. Per K block a CTA streams
 // (2 * 128 + 2 * BN/2) x 128 bytes instead of (2 * 128 + 2 * BN) x 128 for
 // the same 128 x BN outputs of its own: the B tile crosses from L2 once per
-// pair. Each CTA loads its own halves by TMA (no multicast), completing on
+// pair. Each CTA loads its own halves by plain TMA tile loads, completing on
 // the leader CTA's stage barrier; the leader's MMA warp issues the MMAs and
 // signals both CTAs' barriers (stage free, accumulator ready) at once; each
 // CTA drains its own 128 TMEM lanes (its 128 tile rows) and tells the
