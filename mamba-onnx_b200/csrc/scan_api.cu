@@ -23,7 +23,8 @@ using mamba_scan::TmaMaps;
 
 constexpr int kRows = 32;
 constexpr int kTile = 16;
-constexpr int64_t kMinChunk = 32;  // chunks are multiples of 32 steps (two tiles), at least one
+constexpr int64_t kMinChunk = 16;  // chunks are multiples of 16 steps (one tile), at least one
+constexpr int64_t kMinSplit = 32;  // sequences up to this many steps are never split
 
 thread_local std::string t_last_error;
 
@@ -66,8 +67,10 @@ int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
 //   wave of R row tiles (if small enough) is split into c chunks, about one
 //   per sub-partition: the tail then costs an aggregate pass and a chunk
 //   pass of ~1/c of a row tile each instead of a whole row tile.
-// Chunks are multiples of 32 steps, so every chunk but the last starts and
-// ends on a tile boundary.
+// Chunks are multiples of 16 steps (one tile), so every chunk but the last
+// starts and ends on a tile boundary. (Rounding them to 32 instead left the
+// Mamba-130m layer, 1x1536x1024, at 16 chunks of 64 steps, 36.1 us per
+// FusedExact call, against 22 chunks of 48 steps, 30.0 us.)
 Plan make_plan(int64_t batch, int64_t dim, int64_t seqlen, int sms, int slots) {
   Plan pl;
   const int64_t N = batch * ((dim + kRows - 1) / kRows);
@@ -75,7 +78,7 @@ Plan make_plan(int64_t batch, int64_t dim, int64_t seqlen, int sms, int slots) {
   const int64_t wave = std::max<int64_t>(1, (int64_t)slots * sms);
   pl.n_full = N;
   pl.chunk_len = seqlen;
-  if (N <= 0 || seqlen <= kMinChunk) return pl;
+  if (N <= 0 || seqlen <= kMinSplit) return pl;
   int64_t tail = 0, want = 0;
   if (N < subparts) {
     tail = N;
