@@ -278,6 +278,8 @@ def main():
                     help="profiling helper: warmup + steps calls of the tensor-core 3xTF32 "
                          "GEMM on random [M,K] x [N,K] operands; nothing timed")
     args = ap.parse_args()
+    if args.case and not args.ncu_case:
+        ap.error("--case is a profiling helper: use it with --ncu-case")
     args.warmup = max(3, args.warmup)
     if args.steps is None:
         args.steps = 20 if args.impl == "reference" else 2000
