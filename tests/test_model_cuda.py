@@ -60,6 +60,20 @@ def test_small_model_matches_transformers(cuda_device):
         assert _normrel(ours(ids), _hf_logits(hf, ids)) < 1e-5, (batch, L)
 
 
+def test_batched_forward_equals_each_sequence_alone(cuda_device):
+    """Mamba-130m widths (2 blocks), batch 3 x 256 tokens: out_proj splits K
+    through one shared workspace per batch entry in turn, and the scans'
+    chunk plans differ from the single-sequence ones; every sequence's logits
+    must match its own batch-1 forward."""
+    cfg = MambaConfig(n_layer=2)
+    model = MambaLM(cfg).init_random(4).to(cuda_device)
+    ids = _ids(cfg.vocab_size, 256, 11, cuda_device, batch=3)
+    batched = model(ids)
+    for b in range(3):
+        alone = model(ids[b:b + 1])
+        assert _normrel(batched[b:b + 1], alone) < 1e-5, b
+
+
 @pytest.mark.parametrize("L", [64, 1024])
 def test_mamba_130m_matches_transformers_float64(cuda_device, L):
     """L = 1024, batch 1 is the Mamba-130m forward workload (24 blocks)."""
