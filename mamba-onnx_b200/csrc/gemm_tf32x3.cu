@@ -217,7 +217,9 @@ template <int kCols>
 __device__ __forceinline__ void store_sums(const GemmParams& p, float* c,
                                            const float2 (&acc)[kCols / 2], int64_t m_base,
                                            int64_t n_base, float* scratch, int lane) {
-  constexpr int kBatch = 16;
+  // elements per batch of reads: 8 keeps the 576-thread 256-wide pair tile
+  // (96 registers a thread) from spilling (16: LM head 386 -> 349 us at 8)
+  constexpr int kBatch = 8;
   if (p.ldc_m == 1) {
     const int64_t m = m_base + lane;
     const bool m_ok = m < p.M;
