@@ -773,9 +773,11 @@ __global__ void __launch_bounds__(kDtThreads)
     __syncthreads();
 #pragma unroll 8
     for (int k = 0; k < kn; ++k) {
-      const float4 wv = *reinterpret_cast<const float4*>(&ws[k][dt_swz(4 * ty, k)]);
-      const float4 x0 = *reinterpret_cast<const float4*>(&xs[k][dt_swz(4 * tx, k)]);
-      const float4 x1 = *reinterpret_cast<const float4*>(&xs[k][dt_swz(32 + 4 * tx, k)]);
+      // dt_swz of these 4-aligned columns: the group index XOR (k / 4) % 8
+      const int f = (k >> 2) & 7;
+      const float4 wv = *reinterpret_cast<const float4*>(&ws[k][4 * (ty ^ f)]);
+      const float4 x0 = *reinterpret_cast<const float4*>(&xs[k][4 * (tx ^ f)]);
+      const float4 x1 = *reinterpret_cast<const float4*>(&xs[k][4 * ((8 + tx) ^ f)]);
       const float wi[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
