@@ -196,3 +196,34 @@ def test_gemm_split_k_matches_float64(cuda_device, M, N, K, tc, acc):
     with pytest.raises(RuntimeError, match="workspace"):
         run(ws[: need - 16])
     assert cuda.check_device_error() == 0
+
+
+def test_gemm_split_k_strided_c_distinct_c_in_and_reused_workspace(cuda_device):
+    """Split K into a C with padded rows (not the partials' compact layout:
+    the element-wise reduction) from a C_in that is not C, then a different
+    product through the same workspace: each result matches its unsplit
+    product to fp32 rounding, and C_in is left untouched."""
+    dev = cuda_device
+    M, N, K = 768, 1000, 1536
+    ws = torch.empty(max(cuda.gemm_workspace_size(M, N, K), cuda.gemm_workspace_size(80, 1024, 1536)),
+                     dtype=torch.uint8, device=dev)
+    assert cuda.gemm_workspace_size(M, N, K) > 0
+    sa, sb = cuda.split_tf32(_rand((M, K), 31, dev)), cuda.split_tf32(_rand((N, K), 32, dev, 0.05))
+    c_in = _rand((M, N + 5), 33, dev)[:, :N]  # row stride N + 5
+    keep = c_in.clone()
+    c = torch.full((M, N + 5), float("nan"), device=dev)[:, :N]  # C_in shares C's strides
+    cuda.gemm_tf32x3(sa, sb, c, c_in=c_in, workspace=ws)
+    assert torch.equal(c_in, keep)
+    unsplit = torch.empty(M, N + 5, device=dev)[:, :N]
+    cuda.gemm_tf32x3(sa, sb, unsplit, c_in=c_in)
+    bound = (sa.hi[:, :K].double().abs() @ sb.hi[:, :K].double().abs().t()) + keep.double().abs()
+    assert float(((c.double() - unsplit.double()).abs() / (bound + 1e-30)).max()) <= 2e-6
+    # another product through the same workspace, which still holds the first one's partials
+    sx, sy = cuda.split_tf32(_rand((80, 1536), 34, dev)), cuda.split_tf32(_rand((1024, 1536), 35, dev))
+    c2 = torch.empty(1024, 80, device=dev)
+    cuda.gemm_tf32x3(sx, sy, c2, transpose_c=True, workspace=ws)
+    u2 = torch.empty_like(c2)
+    cuda.gemm_tf32x3(sx, sy, u2, transpose_c=True)
+    b2 = (sx.hi[:, :1536].double().abs() @ sy.hi[:, :1536].double().abs().t()).t()
+    assert float(((c2.double() - u2.double()).abs() / (b2 + 1e-30)).max()) <= 2e-6
+    assert cuda.check_device_error() == 0
